@@ -1,0 +1,197 @@
+/*
+ * ww_trt_plugins.h -- C ABI of the B200-native stereo cost-volume front end.
+ *
+ * One shared library, whirlwind_trt_plugins_b200/libww_trt_plugins.so, built
+ * for sm_100a.  Every entry point is `extern "C"`, takes plain pointers and
+ * sizes, never throws, never synchronises the device and never allocates
+ * device memory; kernels are enqueued on `stream` (a cudaStream_t passed as
+ * void*, NULL = legacy default stream).  Device pointers are CUDA device
+ * memory of the current device.
+ *
+ * Reference interfaces replaced (paths relative to the reference project,
+ * IntelligentRoboticsLab/whirlwind_trt_plugins):
+ *   ww_corr_volume            whirlwind::launchCorrVolume<T>
+ *                             src/plugins/corr_volume/corr_volume_kernel.hpp:17-27
+ *   ww_cost_stem3d_ref3       whirlwind::launchCostStem3D
+ *                             src/plugins/cost_stem_3d/cost_stem_3d_kernel.hpp:17-30
+ *   ww_plugin_*               the IPluginV3 methods of CorrVolumePlugin
+ *                             (src/plugins/corr_volume/corr_volume.cpp:28-139) and
+ *                             CostStem3DPlugin (src/plugins/cost_stem_3d/cost_stem_3d.cpp:19-97),
+ *                             with TensorRT types replaced by ww_tensor_desc_t
+ * Extensions with no reference symbol (group-wise correlation fused with a
+ * single G -> Cout 3-D conv stem):
+ *   ww_cost_stem3d            generalised 3-input CostStem3D (Cin -> Cout)
+ *   ww_corr_cost_stem3d       fused CorrVolume -> CostStem3D ("CorrCostStem3D")
+ *   ww_corr_cost_stem3d_band  the same over a band of image rows (multi-GPU sharding)
+ *
+ * Status codes: 0 on success.  The plugin-level ww_plugin_*_enqueue calls
+ * return exactly what IPluginV3OneRuntime::enqueue returns in the reference
+ * (0 success, 1 failure; corr_volume.cpp:150-177).  The kernel-level calls
+ * return a ww_status_t; on a CUDA launch failure they print
+ * "[ww_trt_plugins] <function>: CUDA launch failed: <reason>" to stderr, as
+ * the reference's lastLaunchError does (src/common/cuda_check.hpp:15-23).
+ */
+#ifndef WW_TRT_PLUGINS_H
+#define WW_TRT_PLUGINS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WW_ABI_VERSION 1
+
+typedef enum ww_status {
+    WW_SUCCESS = 0,
+    WW_ERR_LAUNCH = 1,        /* a CUDA launch or runtime call failed            */
+    WW_ERR_INVALID_SHAPE = 2, /* a size is negative, zero where it may not be, or inconsistent */
+    WW_ERR_INVALID_DTYPE = 3, /* dtype not accepted by this entry point          */
+    WW_ERR_NULL_POINTER = 4,  /* a required pointer is NULL                      */
+    WW_ERR_UNSUPPORTED = 5,   /* valid request outside this build's limits       */
+    WW_ERR_MISALIGNED = 6,    /* a pointer lacks the alignment the kernel needs  */
+    WW_ERR_DEVICE = 7         /* no usable sm_100 device is current              */
+} ww_status_t;
+
+/* Same numeric values as nvinfer1::DataType::kFLOAT / kHALF. */
+typedef enum ww_dtype { WW_DTYPE_FLOAT = 0, WW_DTYPE_HALF = 1 } ww_dtype_t;
+
+/* Activation of the generalised / fused stem. */
+typedef enum ww_act { WW_ACT_RELU = 0, WW_ACT_RELU6 = 1 } ww_act_t;
+
+/* Tensor format, same value as nvinfer1::TensorFormat::kLINEAR. */
+#define WW_FORMAT_LINEAR 0
+
+const char* ww_status_string(int status);
+int ww_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * CorrVolume
+ *   out[b, g, d, h, w] = mean_{c in group g} left[b, c, h, w] * right[b, c, h, w - d]
+ *   = +0 where w - d < 0.
+ * left, right : [B, C, H, W]   dtype WW_DTYPE_HALF or WW_DTYPE_FLOAT
+ * out         : [B, G, D, H, W] same dtype (G == 1 is the reference [B, D, H, W])
+ * G divides C.  fp32 sum over the group's channels in channel order; the mean
+ * is taken exactly as the reference kernel the call would run takes it
+ * (acc / C or acc * (1/C)), so results are bit-identical to the reference
+ * called once per (b, g).
+ * Replaces whirlwind::launchCorrVolume<T> (corr_volume_kernel.hpp:17-27).
+ * ------------------------------------------------------------------------- */
+int ww_corr_volume(const void* left, const void* right, void* out, int dtype,
+                   int B, int C, int H, int W, int D, int G, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * CostStem3D, reference 7-input form: three Conv3d 3x3x3 pad 1 (1->4->4->1),
+ * folded-BN bias, ReLU6, fp16 intermediates.  All fp16.
+ * in, out : [B, 1, D, H, W];  w0 [4,1,3,3,3] b0 [4] w1 [4,4,3,3,3] b1 [4]
+ * w2 [1,4,3,3,3] b2 [1].  Every batch item is computed (the reference kernel
+ * writes batch 0 only, cost_stem_3d_kernel.cu:92).
+ * Replaces whirlwind::launchCostStem3D (cost_stem_3d_kernel.hpp:17-30).
+ * ------------------------------------------------------------------------- */
+int ww_cost_stem3d_ref3(const void* in, void* out,
+                        const void* w0, const void* b0, const void* w1, const void* b1,
+                        const void* w2, const void* b2,
+                        int B, int D, int H, int W, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Generalised CostStem3D (extension, 3-input form): one Conv3d 3x3x3 pad 1,
+ * Cin -> Cout, + bias, ReLU or ReLU6.  All fp16, fp32 accumulation on the
+ * tensor cores.
+ * vol [B, Cin, D, H, W], w [Cout, Cin, 3, 3, 3] (BN already folded, see
+ * ww_fold_bn_f16), b [Cout], out [B, Cout, D, H, W].
+ * ------------------------------------------------------------------------- */
+int ww_cost_stem3d(const void* vol, const void* w, const void* b, void* out,
+                   int B, int Cin, int Cout, int D, int H, int W, int act, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused CorrVolume -> CostStem3D (extension, "CorrCostStem3D"):
+ *   vol = ww_corr_volume(left, right, G groups, D disparities)   (fp16, never stored)
+ *   out = ww_cost_stem3d(vol, w, b, act)                          [B, Cout, D, H, W]
+ * left, right [B, C, H, W] fp16; w [Cout, G, 3, 3, 3] fp16; b [Cout] fp16.
+ * ------------------------------------------------------------------------- */
+int ww_corr_cost_stem3d(const void* left, const void* right, const void* w, const void* b,
+                        void* out, int B, int C, int G, int H, int W, int D, int Cout,
+                        int act, void* stream);
+
+/* Row-band form of ww_corr_cost_stem3d for sharding one image pair across
+ * devices.  `left`/`right` hold image rows [in_row0, in_row0 + in_rows) of an
+ * H-row image ([B, C, in_rows, W]); `out` receives rows
+ * [out_row0, out_row0 + out_rows) ([B, Cout, D, out_rows, W]).  The input
+ * band must cover [out_row0 - 1, out_row0 + out_rows + 1) clipped to [0, H)
+ * (a one-row halo each side).  Rows outside [0, H) are the conv's zero
+ * padding, exactly as in the unsharded call. */
+int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w, const void* b,
+                             void* out, int B, int C, int G, int H, int W, int D, int Cout,
+                             int act, int in_row0, int in_rows, int out_row0, int out_rows,
+                             void* stream);
+
+/* BatchNorm folding on the host: w16[o, :] = fp16(w[o, :] * scale[o]) computed in
+ * fp32, b16[o] = fp16(bias[o]); k = Cin * 27.  Host memory only. */
+int ww_fold_bn_f16(const float* w, const float* scale, const float* bias, int cout, int k,
+                   uint16_t* w16, uint16_t* b16);
+
+/* ---------------------------------------------------------------------------
+ * Plugin layer without TensorRT.  These carry the logic of the reference
+ * IPluginV3 methods so that the TensorRT shim (csrc/trt/) is a thin
+ * forwarder and so the logic is testable without TensorRT.
+ * ------------------------------------------------------------------------- */
+typedef struct ww_tensor_desc {
+    int32_t nb_dims;
+    int64_t dims[8];
+    int32_t dtype;  /* ww_dtype_t */
+    int32_t format; /* WW_FORMAT_LINEAR */
+} ww_tensor_desc_t;
+
+/* Creator field parsing (plugin_fields.hpp:17-31 semantics): returns the int
+ * value of field `name` among `nb_fields` (names[i], values[i] may be NULL
+ * meaning "absent / no data"), else `fallback`. */
+int ww_plugin_get_int_field(int nb_fields, const char* const* names, const int32_t* const* values,
+                            const char* name, int fallback);
+
+/* "CorrVolume" v"1": field max_disp (default 48) and extension field
+ * num_groups (default 1).  Output [B, max_disp, H, W] (num_groups == 1) or
+ * [B, num_groups, max_disp, H, W].  corr_volume.cpp:94-148. */
+int ww_plugin_corr_volume_output_dtype(int nb_inputs, const int32_t* in_dtypes, int32_t* out_dtype);
+int ww_plugin_corr_volume_output_dims(int max_disp, int num_groups, int nb_inputs,
+                                      const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out);
+int ww_plugin_corr_volume_supports_format(int pos, const ww_tensor_desc_t* in_out,
+                                          int nb_inputs, int nb_outputs);
+/* corr_volume.cpp:150-177: 0 on success, 1 on bad rank, dtype or launch. */
+int ww_plugin_corr_volume_enqueue(int max_disp, int num_groups, const ww_tensor_desc_t* in_desc,
+                                  const void* const* inputs, void* const* outputs, void* stream);
+
+/* "CostStem3D" v"1": no fields in the reference; 7 inputs (reference) or 3
+ * inputs (generalised extension: vol, w, b, with `act` from the optional
+ * extension field "act", default 0 = ReLU; ignored for 7 inputs).  Output
+ * shape = input 0 shape for 7 inputs, [B, Cout, D, H, W] for 3.
+ * cost_stem_3d.cpp:19-73. */
+int ww_plugin_cost_stem3d_output_dims(int nb_inputs, const ww_tensor_desc_t* inputs,
+                                      ww_tensor_desc_t* out);
+int ww_plugin_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out,
+                                          int nb_inputs, int nb_outputs);
+int ww_plugin_cost_stem3d_enqueue(int nb_inputs, int act, const ww_tensor_desc_t* in_desc,
+                                  const void* const* inputs, void* const* outputs, void* stream);
+
+/* "CorrCostStem3D" v"1" (extension): fields max_disp (48), num_groups (1),
+ * act (0 ReLU, 1 ReLU6); inputs left, right [B,C,H,W], w [Cout,G,3,3,3], b [Cout];
+ * output [B, Cout, max_disp, H, W]; fp16 only. */
+int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_inputs,
+                                           const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out);
+int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out,
+                                               int nb_inputs, int nb_outputs);
+int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act,
+                                       const ww_tensor_desc_t* in_desc,
+                                       const void* const* inputs, void* const* outputs,
+                                       void* stream);
+
+/* Device error word written by bounded waits inside the tensor-core kernels
+ * (0 = none).  Reading it synchronises the current device.  Clearing resets
+ * it to 0. */
+int ww_device_error(int* code);
+int ww_clear_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WW_TRT_PLUGINS_H */

@@ -1,0 +1,144 @@
+"""GPU parity of ww_corr_volume (CorrVolume) against the reference's own CUDA
+kernels (golden fixtures and oracle/_ref live) and the CPU oracle.
+Integer-exact bar: outputs must be bit-identical."""
+import numpy as np
+import pytest
+
+from conftest import golden_files, load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ww():
+    import whirlwind_trt_plugins_b200 as ww
+    return ww
+
+
+def _bits(a):
+    a = np.ascontiguousarray(a)
+    return a.view(np.uint16) if a.dtype == np.float16 else a.view(np.uint32)
+
+
+def _run(ww, torch, L, R, D, G=1, offset=0):
+    """Run the product kernel; `offset` shifts the device pointers by that many
+    elements to exercise the unaligned path."""
+    dev = torch.device("cuda:0")
+    tl = torch.from_numpy(np.ascontiguousarray(L)).to(dev)
+    tr = torch.from_numpy(np.ascontiguousarray(R)).to(dev)
+    if offset:
+        bl = torch.empty(tl.numel() + offset, dtype=tl.dtype, device=dev)
+        br = torch.empty_like(bl)
+        bl[offset:].copy_(tl.flatten())
+        br[offset:].copy_(tr.flatten())
+        tl = bl[offset:].view(tl.shape)
+        tr = br[offset:].view(tr.shape)
+    B, C, H, W = L.shape
+    shape = (B, D, H, W) if G == 1 else (B, G, D, H, W)
+    # canary-padded output: kernel writes must stay inside [pad, pad + n)
+    n = int(np.prod(shape))
+    pad = 64
+    buf = torch.full((n + 2 * pad,), 7.0, dtype=tl.dtype, device=dev)
+    out = buf[pad:pad + n].view(shape)
+    ww.corr_volume(tl, tr, D, G, out=out)
+    torch.cuda.synchronize()
+    host = buf.cpu().numpy()
+    assert np.all(host[:pad] == 7.0) and np.all(host[pad + n:] == 7.0), "write outside the output tensor"
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", [f for f in golden_files() if "corr" in f])
+def test_corr_matches_reference_golden(ww, torch, name):
+    g = load_golden(name)
+    out = _run(ww, torch, g["left"], g["right"], int(g["D"]), int(g["G"]))
+    assert out.shape == g["out"].shape
+    assert np.array_equal(_bits(out), _bits(g["out"])), f"{name}: differs from the reference kernel"
+
+
+def _ref_available():
+    import os
+    import oracle
+    return os.path.exists(oracle.REF_SO)
+
+
+@pytest.mark.parametrize("shape", [
+    (1, 16, 32, 128, 48, 1), (1, 12, 32, 128, 48, 1), (2, 64, 16, 80, 24, 1), (1, 24, 12, 64, 64, 2),
+    (1, 320, 16, 160, 48, 40), (2, 64, 12, 128, 32, 16), (1, 32, 7, 40, 30, 4), (1, 8, 3, 200, 36, 1),
+])
+def test_corr_matches_reference_live(ww, torch, orc, shape):
+    if not _ref_available():
+        pytest.skip("oracle/_ref/libww_ref.so not built")
+    B, C, H, W, D, G = shape
+    rng = np.random.default_rng(sum(shape))
+    L = rng.standard_normal((B, C, H, W)).astype(np.float16)
+    R = rng.standard_normal((B, C, H, W)).astype(np.float16)
+    dev = torch.device("cuda:0")
+    tl, tr = torch.from_numpy(L).to(dev), torch.from_numpy(R).to(dev)
+    ref = torch.full((B, G, D, H, W), float("nan"), dtype=torch.float16, device=dev)
+    rc = orc.ref_lib().wwref_corr_volume_grouped_f16(tl.data_ptr(), tr.data_ptr(), ref.data_ptr(), B, C, H, W, D,
+                                                      G, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    out = _run(ww, torch, L, R, D, G)
+    assert np.array_equal(_bits(out).reshape(-1), _bits(ref.cpu().numpy()).reshape(-1))
+
+
+@pytest.mark.parametrize("cfg_id", [1, 2, 3, 5])
+def test_corr_configs_match_oracle(ww, torch, orc, cfg_id):
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[cfg_id]
+    if cfg_id != 1:
+        cfg = cfg.scaled(H=min(cfg.H, 12), B=min(cfg.B, 2))
+    x = make_inputs(cfg)
+    out = _run(ww, torch, x["left"], x["right"], cfg.D, cfg.G)
+    if cfg.dtype == "f32":
+        ref = orc.corr_f32(x["left"], x["right"], cfg.D, cfg.G)
+    else:
+        ref = orc.corr_f16(x["left"], x["right"], cfg.D, cfg.G)
+    assert np.array_equal(_bits(out), _bits(ref))
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, C=4, H=1, W=5, D=1, G=1),          # minimal
+    dict(B=1, C=8, H=2, W=6, D=20, G=2),          # D > W
+    dict(B=3, C=6, H=5, W=37, D=13, G=3),         # ragged W, odd D
+    dict(B=1, C=40, H=3, W=131, D=70, G=5),       # several column tiles, several disparity bands
+    dict(B=1, C=17, H=2, W=16, D=8, G=17),        # one channel per group
+])
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_corr_edge_cases(ww, torch, orc, case, dtype):
+    rng = np.random.default_rng(case["W"] * 7 + case["D"])
+    shp = (case["B"], case["C"], case["H"], case["W"])
+    L = rng.standard_normal(shp).astype(dtype)
+    R = rng.standard_normal(shp).astype(dtype)
+    out = _run(ww, torch, L, R, case["D"], case["G"])
+    if dtype == np.float32:
+        ref = orc.corr_f32(L, R, case["D"], case["G"])
+    else:
+        ref = orc.corr_f16(L, R, case["D"], case["G"])
+    assert np.array_equal(_bits(out), _bits(ref))
+    # w - d < 0 is exactly +0
+    o = out.reshape(case["B"], case["G"], case["D"], case["H"], case["W"])
+    for d in range(min(case["D"], case["W"])):
+        assert not np.any(_bits(o[:, :, d, :, :d]))
+
+
+def test_corr_unaligned_pointers(ww, torch, orc):
+    rng = np.random.default_rng(99)
+    L = rng.standard_normal((1, 16, 4, 64)).astype(np.float16)
+    R = rng.standard_normal((1, 16, 4, 64)).astype(np.float16)
+    out = _run(ww, torch, L, R, 24, 2, offset=1)
+    ref = orc.corr_f16(L, R, 24, 2)
+    assert np.array_equal(_bits(out), _bits(ref))
+
+
+def test_corr_rejects_bad_arguments(ww, torch):
+    dev = torch.device("cuda:0")
+    x = torch.zeros((1, 6, 2, 8), dtype=torch.float16, device=dev)
+    with pytest.raises(ww.WWError):
+        ww.corr_volume(x, x, 4, num_groups=4)

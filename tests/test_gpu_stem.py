@@ -1,0 +1,180 @@
+"""GPU parity of the stems and of the fused front end.
+
+* ww_cost_stem3d_ref3 (reference 7-input CostStem3D): bit-identical to the
+  reference kernel (golden fixtures, live oracle/_ref at B = 1) and to the
+  oracle for B > 1 (the reference kernel only writes batch 0).
+* ww_cost_stem3d / ww_corr_cost_stem3d (tensor cores, fp32 accumulation in a
+  different order than the oracle): |out - oracle| <= 2e-2 absolute (fp16
+  tolerance of the north-star contract; values are already normalised by the
+  channel count in the correlation), with the volume itself bit-identical.
+"""
+import numpy as np
+import pytest
+
+from conftest import golden_files, load_golden
+
+pytestmark = pytest.mark.gpu
+
+ATOL_F16 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ww():
+    import whirlwind_trt_plugins_b200 as ww
+    return ww
+
+
+def _t(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(torch.device("cuda:0"))
+
+
+def _u16(a):
+    return np.ascontiguousarray(a).view(np.uint16)
+
+
+# ------------------------------------------------------------------ ref3 stem
+
+@pytest.mark.parametrize("name", [f for f in golden_files() if "stem3" in f])
+def test_ref3_matches_reference_golden(ww, torch, name):
+    g = load_golden(name)
+    ws = [_t(torch, g[k]) for k in ("w0", "b0", "w1", "b1", "w2", "b2")]
+    out = ww.cost_stem3d_ref3(_t(torch, g["vol"]), *ws).cpu().numpy()
+    assert np.array_equal(_u16(out), _u16(g["out"]))
+
+
+def _ref3_weights(rng):
+    return [(rng.standard_normal(n) * s).astype(np.float16) for n, s in
+            ((108, 0.3), (4, 0.2), (432, 0.2), (4, 0.2), (108, 0.2), (1, 0.2))]
+
+
+@pytest.mark.parametrize("shape", [(1, 48, 32, 40), (3, 13, 9, 11), (2, 1, 1, 1), (1, 20, 33, 65)])
+def test_ref3_matches_oracle_all_batches(ww, torch, orc, shape):
+    B, D, H, W = shape
+    rng = np.random.default_rng(D * 31 + W)
+    x = (rng.standard_normal((B, 1, D, H, W)) * 2).astype(np.float16)
+    ws = _ref3_weights(rng)
+    out = ww.cost_stem3d_ref3(_t(torch, x), *[_t(torch, w) for w in ws]).cpu().numpy()
+    ref = orc.stem_ref3(x, *ws)
+    assert np.array_equal(_u16(out), _u16(ref))
+
+
+def test_ref3_matches_reference_live_b1(ww, torch, orc):
+    import os
+    if not os.path.exists(orc.REF_SO):
+        pytest.skip("oracle/_ref/libww_ref.so not built")
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((1, 1, 48, 32, 40)) * 2).astype(np.float16)
+    ws = _ref3_weights(rng)
+    tx, tws = _t(torch, x), [_t(torch, w) for w in ws]
+    ref = torch.empty_like(tx)
+    rc = orc.ref_lib().wwref_cost_stem3d(tx.data_ptr(), ref.data_ptr(), *[w.data_ptr() for w in tws], 1, 48, 32, 40,
+                                         torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    out = ww.cost_stem3d_ref3(tx, *tws)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+# ------------------------------------------------------ generalised stem (TC)
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, Cin=40, Cout=32, D=48, H=5, W=16),
+    dict(B=2, Cin=8, Cout=16, D=64, H=4, W=24),
+    dict(B=1, Cin=32, Cout=32, D=48, H=3, W=8),
+    dict(B=1, Cin=16, Cout=16, D=32, H=6, W=13),     # ragged W
+    dict(B=1, Cin=5, Cout=7, D=20, H=4, W=9),        # padded channels, Cout, D
+    dict(B=1, Cin=24, Cout=20, D=16, H=1, W=8),      # H = 1
+    dict(B=1, Cin=12, Cout=32, D=80, H=3, W=17),     # five M-blocks along D
+])
+@pytest.mark.parametrize("act", [0, 1])
+def test_stem_tc_matches_oracle(ww, torch, orc, case, act):
+    B, Cin, Cout, D, H, W = (case[k] for k in ("B", "Cin", "Cout", "D", "H", "W"))
+    rng = np.random.default_rng(Cin * 100 + Cout + D)
+    vol = (rng.standard_normal((B, Cin, D, H, W)) * 0.5).astype(np.float16)
+    w = (rng.standard_normal((Cout, Cin, 3, 3, 3)) * 0.05).astype(np.float16)
+    b = (rng.standard_normal(Cout) * 0.1).astype(np.float16)
+    out = ww.cost_stem3d(_t(torch, vol), _t(torch, w), _t(torch, b), act=act).cpu().numpy().astype(np.float32)
+    ref = orc.stem(vol, w, b, act=act, acc_mode=orc.ACC_F64).astype(np.float32)
+    err = np.abs(out - ref).max()
+    assert err <= ATOL_F16, f"max abs err {err}"
+    assert np.all(np.isfinite(out))
+
+
+# ------------------------------------------------------------ fused front end
+
+def _fused(ww, torch, x, cfg, act=0):
+    return ww.corr_cost_stem3d(_t(torch, x["left"]), _t(torch, x["right"]), _t(torch, x["w"]), _t(torch, x["b"]),
+                               cfg.D, cfg.G, act=act)
+
+
+@pytest.mark.parametrize("cfg_id", [2, 3, 4, 5])
+def test_fused_configs_match_oracle(ww, torch, orc, cfg_id):
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[cfg_id]
+    cfg = cfg.scaled(B=min(cfg.B, 2), H=min(cfg.H, 10), W=min(cfg.W, 64))
+    x = make_inputs(cfg)
+    out = _fused(ww, torch, x, cfg).cpu().numpy().astype(np.float32)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=orc.ACC_F64)
+    err = np.abs(out - ref.astype(np.float32)).max()
+    assert err <= ATOL_F16, f"max abs err {err}"
+
+
+def test_fused_equals_unfused_composition(ww, torch, orc):
+    """corr -> stem through HBM and the fused kernel give identical bits: the
+    fused volume is the CorrVolume result bit for bit."""
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[2].scaled(H=9, W=40)
+    x = make_inputs(cfg)
+    tl, tr, tw, tb = (_t(torch, x[k]) for k in ("left", "right", "w", "b"))
+    fused = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+    vol = ww.corr_volume(tl, tr, cfg.D, cfg.G)
+    unfused = ww.cost_stem3d(vol, tw, tb)
+    assert torch.equal(fused.view(torch.int16), unfused.view(torch.int16))
+    ref_vol = orc.corr_f16(x["left"], x["right"], cfg.D, cfg.G)
+    assert np.array_equal(_u16(vol.cpu().numpy()), _u16(ref_vol))
+
+
+@pytest.mark.parametrize("cfg_id", [2, 5])
+def test_fused_full_size_matches_oracle(ww, torch, orc, cfg_id):
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[cfg_id]
+    x = make_inputs(cfg)
+    out = _fused(ww, torch, x, cfg).cpu().numpy().astype(np.float32)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=orc.ACC_F32_SEQ)
+    err = np.abs(out - ref.astype(np.float32)).max()
+    assert err <= ATOL_F16, f"max abs err {err}"
+
+
+def test_fused_band_stitches_to_full(ww, torch):
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[3].scaled(B=1, H=23, W=40)
+    x = make_inputs(cfg)
+    tl, tr, tw, tb = (_t(torch, x[k]) for k in ("left", "right", "w", "b"))
+    full = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+    parts = []
+    for (r0, r1) in ((0, 7), (7, 8), (8, 23)):
+        i0, i1 = max(0, r0 - 1), min(cfg.H, r1 + 1)
+        band_l = tl[:, :, i0:i1].contiguous()
+        band_r = tr[:, :, i0:i1].contiguous()
+        parts.append(ww.corr_cost_stem3d_band(band_l, band_r, tw, tb, cfg.D, cfg.G, cfg.H, i0, r0, r1 - r0))
+    stitched = torch.cat(parts, dim=3)
+    assert torch.equal(stitched.view(torch.int16), full.view(torch.int16))
+
+
+def test_fused_relu6(ww, torch, orc):
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[5].scaled(B=1, H=6, W=24)
+    x = make_inputs(cfg)
+    x["b"] = (x["b"].astype(np.float32) + 5.0).astype(np.float16)  # push values past 6
+    out = _fused(ww, torch, x, cfg, act=1).cpu().numpy().astype(np.float32)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, act=1).astype(np.float32)
+    assert out.max() <= 6.0 and np.abs(out - ref).max() <= ATOL_F16
+
+
+def test_no_device_error_recorded(ww, torch):
+    assert ww.device_error() == 0

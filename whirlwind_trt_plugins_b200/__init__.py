@@ -1,0 +1,242 @@
+"""B200-native stereo cost-volume front end (CorrVolume -> CostStem3D).
+
+Python host side over the C ABI of ``libww_trt_plugins.so``
+(``include/ww_trt_plugins.h``).  torch supplies device memory and streams;
+every computation runs in the library's sm_100a kernels.  There is no CPU
+fallback: importing this package fails loudly when the library is missing,
+and every call raises ``WWError`` when the library rejects it.
+
+Operators (reference interfaces in parentheses, paths relative to the
+reference project):
+
+* ``corr_volume(left, right, max_disp, num_groups=1)``  -- CorrVolume
+  (``src/plugins/corr_volume/corr_volume_kernel.hpp:17-27``)
+* ``cost_stem3d_ref3(vol, w0, b0, w1, b1, w2, b2)``     -- CostStem3D 7-input form
+  (``src/plugins/cost_stem_3d/cost_stem_3d_kernel.hpp:17-30``)
+* ``cost_stem3d(vol, w, b, act)``                      -- generalised 3-input stem
+* ``corr_cost_stem3d(left, right, w, b, max_disp, num_groups, act)`` -- fused op
+* ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
+
+The plugin-level classes mirroring the reference's IPluginV3 plugins live in
+``whirlwind_trt_plugins_b200.plugins``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+__all__ = [
+    "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "cost_stem3d",
+    "corr_cost_stem3d", "corr_cost_stem3d_band", "fold_bn", "device_error", "clear_device_error",
+    "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF",
+]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libww_trt_plugins.so")
+
+DTYPE_FLOAT = 0
+DTYPE_HALF = 1
+ACT_RELU = 0
+ACT_RELU6 = 1
+
+STATUS = {
+    0: "success", 1: "CUDA launch or runtime call failed", 2: "invalid tensor shape",
+    3: "unsupported data type", 4: "null pointer", 5: "request outside the supported limits",
+    6: "pointer not aligned as required", 7: "no usable sm_100 device",
+}
+
+
+class WWError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        super().__init__(f"{fn} failed: status {status} ({STATUS.get(status, 'unknown')})")
+        self.status = status
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m whirlwind_trt_plugins_b200.build` "
+            "(nvcc, sm_100a). There is no CPU fallback.")
+    L = ctypes.CDLL(LIB_PATH)
+    p, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    L.ww_status_string.restype = ctypes.c_char_p
+    L.ww_status_string.argtypes = [i]
+    L.ww_abi_version.restype = i
+    L.ww_corr_volume.argtypes = [p, p, p] + [i] * 7 + [p]
+    L.ww_cost_stem3d_ref3.argtypes = [p] * 8 + [i] * 4 + [p]
+    L.ww_cost_stem3d.argtypes = [p, p, p, p] + [i] * 7 + [p]
+    L.ww_corr_cost_stem3d.argtypes = [p, p, p, p, p] + [i] * 8 + [p]
+    L.ww_corr_cost_stem3d_band.argtypes = [p, p, p, p, p] + [i] * 12 + [p]
+    L.ww_fold_bn_f16.argtypes = [p, p, p, i, i, p, p]
+    L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    L.ww_clear_device_error.argtypes = []
+    del f
+    return L
+
+
+_lib = _load()
+
+
+def lib() -> ctypes.CDLL:
+    return _lib
+
+
+def _check(fn: str, status: int) -> None:
+    if status != 0:
+        raise WWError(fn, status)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _stream_ptr(stream) -> int | None:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _dev(t, name: str, dtype=None):
+    torch = _torch()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    return t
+
+
+def corr_volume(left, right, max_disp: int, num_groups: int = 1, out=None, stream=None):
+    """Group-wise correlation volume.
+
+    left, right: [B, C, H, W] fp16 or fp32 CUDA tensors.  Returns
+    [B, max_disp, H, W] for num_groups == 1 (the reference CorrVolume output),
+    else [B, num_groups, max_disp, H, W]."""
+    torch = _torch()
+    _dev(left, "left")
+    _dev(right, "right", left.dtype)
+    if left.shape != right.shape or left.dim() != 4:
+        raise ValueError("left/right must both be [B, C, H, W]")
+    dt = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}.get(left.dtype)
+    if dt is None:
+        raise TypeError("corr_volume supports fp16 and fp32")
+    B, C, H, W = left.shape
+    shape = (B, max_disp, H, W) if num_groups == 1 else (B, num_groups, max_disp, H, W)
+    if out is None:
+        out = torch.empty(shape, dtype=left.dtype, device=left.device)
+    _dev(out, "out", left.dtype)
+    _check("ww_corr_volume", _lib.ww_corr_volume(left.data_ptr(), right.data_ptr(), out.data_ptr(), dt,
+                                                 B, C, H, W, max_disp, num_groups, _stream_ptr(stream)))
+    return out
+
+
+def cost_stem3d_ref3(vol, w0, b0, w1, b1, w2, b2, out=None, stream=None):
+    """The reference CostStem3D (1->4->4->1, ReLU6), every batch item.  All fp16."""
+    torch = _torch()
+    _dev(vol, "vol", torch.float16)
+    ws = [_dev(x, n, torch.float16) for x, n in zip((w0, b0, w1, b1, w2, b2), ("w0", "b0", "w1", "b1", "w2", "b2"))]
+    for x, n in zip(ws, (108, 4, 432, 4, 108, 1)):
+        if x.numel() != n:
+            raise ValueError("CostStem3D weight/bias has the wrong size")
+    if vol.dim() != 5 or vol.shape[1] != 1:
+        raise ValueError("vol must be [B, 1, D, H, W]")
+    B, _, D, H, W = vol.shape
+    if out is None:
+        out = torch.empty_like(vol)
+    _dev(out, "out", torch.float16)
+    _check("ww_cost_stem3d_ref3", _lib.ww_cost_stem3d_ref3(vol.data_ptr(), out.data_ptr(),
+                                                           *[x.data_ptr() for x in ws], B, D, H, W,
+                                                           _stream_ptr(stream)))
+    return out
+
+
+def cost_stem3d(vol, w, b, act: int = ACT_RELU, out=None, stream=None):
+    """Generalised stem: Conv3d 3x3x3 pad 1 Cin->Cout + bias + ReLU/ReLU6 on tensor cores."""
+    torch = _torch()
+    _dev(vol, "vol", torch.float16)
+    _dev(w, "w", torch.float16)
+    _dev(b, "b", torch.float16)
+    if vol.dim() != 5:
+        raise ValueError("vol must be [B, Cin, D, H, W]")
+    B, Cin, D, H, W = vol.shape
+    Cout = b.numel()
+    if w.numel() != Cout * Cin * 27:
+        raise ValueError("w must be [Cout, Cin, 3, 3, 3]")
+    if out is None:
+        out = torch.empty((B, Cout, D, H, W), dtype=torch.float16, device=vol.device)
+    _dev(out, "out", torch.float16)
+    _check("ww_cost_stem3d", _lib.ww_cost_stem3d(vol.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                                 B, Cin, Cout, D, H, W, act, _stream_ptr(stream)))
+    return out
+
+
+def corr_cost_stem3d(left, right, w, b, max_disp: int, num_groups: int, act: int = ACT_RELU, out=None,
+                     stream=None):
+    """Fused group-wise correlation + stem; the volume never leaves the SM.
+
+    left, right [B, C, H, W] fp16, w [Cout, G, 3, 3, 3] fp16, b [Cout] fp16.
+    Returns [B, Cout, max_disp, H, W] fp16."""
+    torch = _torch()
+    for t, n in ((left, "left"), (right, "right"), (w, "w"), (b, "b")):
+        _dev(t, n, torch.float16)
+    if left.shape != right.shape or left.dim() != 4:
+        raise ValueError("left/right must both be [B, C, H, W]")
+    B, C, H, W = left.shape
+    Cout = b.numel()
+    if w.numel() != Cout * num_groups * 27:
+        raise ValueError("w must be [Cout, num_groups, 3, 3, 3]")
+    if out is None:
+        out = torch.empty((B, Cout, max_disp, H, W), dtype=torch.float16, device=left.device)
+    _dev(out, "out", torch.float16)
+    _check("ww_corr_cost_stem3d", _lib.ww_corr_cost_stem3d(
+        left.data_ptr(), right.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+        B, C, num_groups, H, W, max_disp, Cout, act, _stream_ptr(stream)))
+    return out
+
+
+def corr_cost_stem3d_band(left_band, right_band, w, b, max_disp: int, num_groups: int, H: int,
+                          in_row0: int, out_row0: int, out_rows: int, act: int = ACT_RELU, out=None,
+                          stream=None):
+    """Rows [out_row0, out_row0+out_rows) of the fused op from an input band
+    holding image rows [in_row0, in_row0 + left_band.shape[2])."""
+    torch = _torch()
+    for t, n in ((left_band, "left"), (right_band, "right"), (w, "w"), (b, "b")):
+        _dev(t, n, torch.float16)
+    B, C, in_rows, W = left_band.shape
+    Cout = b.numel()
+    if out is None:
+        out = torch.empty((B, Cout, max_disp, out_rows, W), dtype=torch.float16, device=left_band.device)
+    _dev(out, "out", torch.float16)
+    _check("ww_corr_cost_stem3d_band", _lib.ww_corr_cost_stem3d_band(
+        left_band.data_ptr(), right_band.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+        B, C, num_groups, H, W, max_disp, Cout, act, in_row0, in_rows, out_row0, out_rows,
+        _stream_ptr(stream)))
+    return out
+
+
+def fold_bn(w, scale, bias):
+    """Host BatchNorm fold (numpy): fp16(w * scale[o]) and fp16(bias)."""
+    import numpy as np
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    bias = np.ascontiguousarray(bias, dtype=np.float32)
+    cout = w.shape[0]
+    k = w.size // cout
+    w16 = np.empty(w.shape, dtype=np.uint16)
+    b16 = np.empty((cout,), dtype=np.uint16)
+    _check("ww_fold_bn_f16", _lib.ww_fold_bn_f16(w.ctypes.data, scale.ctypes.data, bias.ctypes.data, cout, k,
+                                                 w16.ctypes.data, b16.ctypes.data))
+    return w16.view(np.float16), b16.view(np.float16)
+
+
+def device_error() -> int:
+    """Error word written by bounded device-side waits (0 = none); synchronises."""
+    code = ctypes.c_int(0)
+    _check("ww_device_error", _lib.ww_device_error(ctypes.byref(code)))
+    return code.value
+
+
+def clear_device_error() -> None:
+    _check("ww_clear_device_error", _lib.ww_clear_device_error())

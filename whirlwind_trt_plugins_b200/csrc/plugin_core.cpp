@@ -1,0 +1,206 @@
+// plugin_core.cpp -- the logic of the reference's IPluginV3 methods for
+// CorrVolume and CostStem3D (and the fused CorrCostStem3D extension), written
+// against plain descriptors (ww_tensor_desc_t) instead of TensorRT types.
+// The TensorRT shim in trt/ forwards each IPluginV3 method here; the tests
+// call these directly.  Nothing here touches the GPU except the *_enqueue
+// functions, and those only after every check has passed.
+#include "../../include/ww_trt_plugins.h"
+
+#include <cstring>
+
+namespace {
+
+bool is_linear_half(const ww_tensor_desc_t& d)
+{
+    return d.format == WW_FORMAT_LINEAR && d.dtype == WW_DTYPE_HALF;
+}
+
+bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffff; }
+
+}  // namespace
+
+extern "C" {
+
+// plugin_fields.hpp:17-31: first field named `name` whose data is non-null.
+int ww_plugin_get_int_field(int nb_fields, const char* const* names, const int32_t* const* values,
+                            const char* name, int fallback)
+{
+    if (names == nullptr || values == nullptr || name == nullptr) return fallback;
+    for (int i = 0; i < nb_fields; ++i) {
+        if (values[i] == nullptr || names[i] == nullptr) continue;
+        if (std::strcmp(names[i], name) == 0) return *values[i];
+    }
+    return fallback;
+}
+
+// ---------------------------------------------------------------- CorrVolume
+
+// corr_volume.cpp:94-103: output type = input 0 type.
+int ww_plugin_corr_volume_output_dtype(int nb_inputs, const int32_t* in_dtypes, int32_t* out_dtype)
+{
+    if (nb_inputs < 1 || in_dtypes == nullptr || out_dtype == nullptr) return 1;
+    *out_dtype = in_dtypes[0];
+    return 0;
+}
+
+// corr_volume.cpp:105-124: [B, max_disp, H, W]; with the num_groups extension
+// and G > 1: [B, G, max_disp, H, W].
+int ww_plugin_corr_volume_output_dims(int max_disp, int num_groups, int nb_inputs,
+                                      const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
+{
+    if (nb_inputs != 2 || inputs == nullptr || out == nullptr) return 1;
+    const ww_tensor_desc_t& in = inputs[0];
+    if (in.nb_dims != 4) return 1;
+    *out = in;
+    if (num_groups <= 1) {
+        out->nb_dims = 4;
+        out->dims[0] = in.dims[0];
+        out->dims[1] = max_disp;
+        out->dims[2] = in.dims[2];
+        out->dims[3] = in.dims[3];
+    } else {
+        out->nb_dims = 5;
+        out->dims[0] = in.dims[0];
+        out->dims[1] = num_groups;
+        out->dims[2] = max_disp;
+        out->dims[3] = in.dims[2];
+        out->dims[4] = in.dims[3];
+    }
+    return 0;
+}
+
+// corr_volume.cpp:126-148: LINEAR only; position 0 fp16 only (advertising
+// fp32 would let TensorRT insert a reformat in front of the fast path); the
+// other input and the output must match position 0.
+int ww_plugin_corr_volume_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                          int nb_outputs)
+{
+    if (in_out == nullptr || nb_inputs != 2 || nb_outputs != 1) return 0;
+    if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
+    const ww_tensor_desc_t& d = in_out[pos];
+    if (d.format != WW_FORMAT_LINEAR) return 0;
+    if (pos == 0) return d.dtype == WW_DTYPE_HALF;
+    return d.dtype == in_out[0].dtype;
+}
+
+// corr_volume.cpp:150-177: rank-4 input, fp16 or fp32, launch; 0 or 1.
+int ww_plugin_corr_volume_enqueue(int max_disp, int num_groups, const ww_tensor_desc_t* in_desc,
+                                  const void* const* inputs, void* const* outputs, void* stream)
+{
+    if (in_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    const ww_tensor_desc_t& d = in_desc[0];
+    if (d.nb_dims != 4) return 1;
+    for (int i = 0; i < 4; ++i)
+        if (!fits_int(d.dims[i])) return 1;
+    if (d.dtype != WW_DTYPE_HALF && d.dtype != WW_DTYPE_FLOAT) return 1;
+    const int G = num_groups <= 0 ? 1 : num_groups;
+    const int st = ww_corr_volume(inputs[0], inputs[1], outputs[0], d.dtype, static_cast<int>(d.dims[0]),
+                                  static_cast<int>(d.dims[1]), static_cast<int>(d.dims[2]),
+                                  static_cast<int>(d.dims[3]), max_disp, G, stream);
+    return st == WW_SUCCESS ? 0 : 1;
+}
+
+// ---------------------------------------------------------------- CostStem3D
+
+// cost_stem_3d.cpp:28-37 (7 inputs: output = input 0 shape) plus the 3-input
+// generalised form (output [B, Cout, D, H, W], Cout = w.dims[0]).
+int ww_plugin_cost_stem3d_output_dims(int nb_inputs, const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
+{
+    if (inputs == nullptr || out == nullptr) return 1;
+    if (nb_inputs == 7) {
+        *out = inputs[0];
+        return 0;
+    }
+    if (nb_inputs == 3) {
+        if (inputs[0].nb_dims != 5 || inputs[1].nb_dims != 5) return 1;
+        *out = inputs[0];
+        out->dims[1] = inputs[1].dims[0];
+        return 0;
+    }
+    return 1;
+}
+
+// cost_stem_3d.cpp:39-48: every position fp16 LINEAR.
+int ww_plugin_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                          int nb_outputs)
+{
+    if (in_out == nullptr || (nb_inputs != 7 && nb_inputs != 3) || nb_outputs != 1) return 0;
+    if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
+    return is_linear_half(in_out[pos]);
+}
+
+// cost_stem_3d.cpp:50-73 (rank-5 input 0, B = d[0], D = d[2], H = d[3],
+// W = d[4]) and the 3-input form (w [Cout, Cin, 3, 3, 3], b [Cout]).
+int ww_plugin_cost_stem3d_enqueue(int nb_inputs, int act, const ww_tensor_desc_t* in_desc,
+                                  const void* const* inputs, void* const* outputs, void* stream)
+{
+    if (in_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    const ww_tensor_desc_t& d = in_desc[0];
+    if (d.nb_dims != 5) return 1;
+    for (int i = 0; i < 5; ++i)
+        if (!fits_int(d.dims[i])) return 1;
+    const int B = static_cast<int>(d.dims[0]), D = static_cast<int>(d.dims[2]);
+    const int H = static_cast<int>(d.dims[3]), W = static_cast<int>(d.dims[4]);
+    int st;
+    if (nb_inputs == 7) {
+        st = ww_cost_stem3d_ref3(inputs[0], outputs[0], inputs[1], inputs[2], inputs[3], inputs[4], inputs[5],
+                                 inputs[6], B, D, H, W, stream);
+    } else if (nb_inputs == 3) {
+        const ww_tensor_desc_t& wd = in_desc[1];
+        if (wd.nb_dims != 5 || wd.dims[1] != d.dims[1] || wd.dims[2] != 3 || wd.dims[3] != 3 || wd.dims[4] != 3)
+            return 1;
+        if (!fits_int(wd.dims[0])) return 1;
+        st = ww_cost_stem3d(inputs[0], inputs[1], inputs[2], outputs[0], B, static_cast<int>(d.dims[1]),
+                            static_cast<int>(wd.dims[0]), D, H, W, act, stream);
+    } else {
+        return 1;
+    }
+    return st == WW_SUCCESS ? 0 : 1;
+}
+
+// ------------------------------------------------------- CorrCostStem3D (new)
+
+int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_inputs,
+                                           const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
+{
+    (void)num_groups;
+    if (nb_inputs != 4 || inputs == nullptr || out == nullptr) return 1;
+    if (inputs[0].nb_dims != 4 || inputs[2].nb_dims != 5) return 1;
+    *out = inputs[0];
+    out->nb_dims = 5;
+    out->dims[0] = inputs[0].dims[0];
+    out->dims[1] = inputs[2].dims[0];
+    out->dims[2] = max_disp;
+    out->dims[3] = inputs[0].dims[2];
+    out->dims[4] = inputs[0].dims[3];
+    return 0;
+}
+
+int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                               int nb_outputs)
+{
+    if (in_out == nullptr || nb_inputs != 4 || nb_outputs != 1) return 0;
+    if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
+    return is_linear_half(in_out[pos]);
+}
+
+int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act, const ww_tensor_desc_t* in_desc,
+                                       const void* const* inputs, void* const* outputs, void* stream)
+{
+    if (in_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    const ww_tensor_desc_t& d = in_desc[0];
+    const ww_tensor_desc_t& wd = in_desc[2];
+    if (d.nb_dims != 4 || wd.nb_dims != 5) return 1;
+    for (int i = 0; i < 4; ++i)
+        if (!fits_int(d.dims[i])) return 1;
+    const int G = num_groups <= 0 ? 1 : num_groups;
+    if (wd.dims[1] != G || wd.dims[2] != 3 || wd.dims[3] != 3 || wd.dims[4] != 3 || !fits_int(wd.dims[0])) return 1;
+    if (d.dtype != WW_DTYPE_HALF) return 1;
+    const int st = ww_corr_cost_stem3d(inputs[0], inputs[1], inputs[2], inputs[3], outputs[0],
+                                       static_cast<int>(d.dims[0]), static_cast<int>(d.dims[1]), G,
+                                       static_cast<int>(d.dims[2]), static_cast<int>(d.dims[3]), max_disp,
+                                       static_cast<int>(wd.dims[0]), act, stream);
+    return st == WW_SUCCESS ? 0 : 1;
+}
+
+}  // extern "C"

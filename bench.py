@@ -1,0 +1,357 @@
+"""Benchmark of the fused stereo front end (group-wise correlation -> 3x3x3
+stem) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+One step = one fused correlation + stem pass (ww_corr_cost_stem3d) over one
+batch of the workload (default: config 2, B=1 C=320 G=40 H=120 W=160 D=48
+Cout=32, fp16).  Under torchrun (N > 1) every rank runs its own batch on its
+own GPU: the path partitions by batch with no exchange, so scaling is weak
+(global batch = N x B) and no collective touches the data path.
+
+Printed (rank 0, one JSON line):
+  value      whole-job cost voxels/s (B*D*H*W per step, summed over ranks),
+             inputs resident in HBM, CUDA-event time of exactly K steps, max
+             over ranks; K steps rotate over input/output sets whose total
+             size exceeds the 126 MB L2, so no step reads another's cache.
+  e2e        the same metric through the public API from pinned HOST buffers:
+             every step copies left/right host->device, runs the op and copies
+             the whole output volume device->host, all inside the timed region.
+  roofline   the fused kernel against the measured B200 peaks
+             (MEASURED_PEAKS.json): algorithmic stem FLOPs / kernel time vs
+             the bf16/fp16 tensor peak, and algorithmic bytes / time vs HBM.
+  cpu_baseline  the CPU oracle (plain-C restatement of the reference's
+             semantics; the reference has no CPU implementation of its own)
+             on a bounded row band of the same workload, all host threads.
+--impl reference times that CPU implementation on the same workload
+(rank 0 only; the other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "cost voxels/s (B*D*H*W) corr+3D stem"
+UNIT = "voxels/s"
+
+# DRAM bytes (read + write) per launch of the fused kernel, from the ncu
+# captures summarised in profiles/ (None until captured for that config).
+NCU_TRAFFIC_BYTES = {}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling driver for ncu: one input set, W + K launches, nothing else")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample_inputs(cfg, rows: int):
+    """Inputs for output rows [0, rows) of batch item 0 (plus the halo row)."""
+    from whirlwind_trt_plugins_b200.configs import make_inputs
+    return make_inputs(cfg.scaled(B=1, H=min(cfg.H, rows + 1)))
+
+
+def cpu_oracle_seconds(cfg, x, rows: int, nthreads: int) -> float:
+    """Wall time of the CPU oracle (corr + stem, fp32 accumulation) on output
+    rows [0, rows) of batch item 0."""
+    import oracle
+    t0 = time.perf_counter()
+    oracle.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=oracle.ACC_F32_SEQ,
+                     rows=(0, rows), nthreads=nthreads)
+    return time.perf_counter() - t0
+
+
+def pick_cpu_rows(cfg, budget_s: float, nthreads: int) -> int:
+    """Rows of batch item 0 whose oracle time is about `budget_s` seconds."""
+    probe = min(cfg.H, 4)
+    dt = cpu_oracle_seconds(cfg, cpu_sample_inputs(cfg, probe), probe, nthreads) / probe
+    return max(1, min(cfg.H, int(budget_s / max(dt, 1e-4))))
+
+
+def cpu_baseline(cfg, budget_s: float = 12.0) -> dict:
+    import oracle
+    n = oracle.nthreads_default()
+    rows = pick_cpu_rows(cfg, budget_s, n)
+    x = cpu_sample_inputs(cfg, rows)
+    dt = cpu_oracle_seconds(cfg, x, rows, n)
+    return {"value": rows * cfg.W * cfg.D / dt, "unit": UNIT, "cores": n, "kind": "port",
+            "sample": f"output rows [0,{rows}) of batch item 0 of {cfg.name}: corr+stem in the C oracle "
+                      f"(fp32 accumulation), {dt:.1f} s"}
+
+
+def run_reference(args, cfg, rank):
+    """Reference arm: the CPU implementation of the path (the oracle port),
+    each step a bounded row band of the workload; the whole run is sized to
+    about two minutes."""
+    if rank != 0:
+        return
+    import oracle
+    n = oracle.nthreads_default()
+    per_step = min(2.0, 120.0 / max(1, args.steps + args.warmup))
+    rows = pick_cpu_rows(cfg, per_step, n)
+    x = cpu_sample_inputs(cfg, rows)
+    for _ in range(args.warmup):
+        cpu_oracle_seconds(cfg, x, rows, n)
+    times = [cpu_oracle_seconds(cfg, x, rows, n) for _ in range(args.steps)]
+    vox = rows * cfg.W * cfg.D
+    value = vox * len(times) / sum(times)
+    sample = f"output rows [0,{rows}) of batch item 0 of {cfg.name} per step (corr+stem, fp32 accumulation)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": {"workload": cfg.name},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": n, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU implementation of this path; its semantics run as the "
+                "plain-C oracle port (oracle/ww_oracle.c) on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    from whirlwind_trt_plugins_b200.configs import CONFIGS
+    cfg = CONFIGS[args.config]
+    if cfg.Cout == 0:
+        raise SystemExit("bench.py measures the fused front end; config %d has no stem" % args.config)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    from whirlwind_trt_plugins_b200.configs import make_inputs_torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- resident inputs: enough rotating sets to exceed L2 ----
+    per_set = cfg.algorithmic_bytes()
+    n_sets = max(2, -(-400 * 2**20 // per_set))  # >= 400 MB in flight
+    n_sets = 1 if args.profile else min(n_sets, 8)
+    sets = []
+    for s in range(n_sets):
+        x = make_inputs_torch(cfg, dev, seed=1000 * rank + 10 * s)
+        out = torch.empty((cfg.B, cfg.Cout, cfg.D, cfg.H, cfg.W), dtype=torch.float16, device=dev)
+        sets.append((x["left"], x["right"], x["w"], x["b"], out))
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        L, R, w, b, out = sets[i % n_sets]
+        ww.corr_cost_stem3d(L, R, w, b, cfg.D, cfg.G, act=cfg.act, out=out, stream=stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        print(f"profile run: {cfg.name}, {args.warmup} + {args.steps} launches of the fused kernel", flush=True)
+        return
+
+    # ---- device-timed value ----
+    with ClockSampler(local) as clk:
+        t_end = time.time() + 1.5          # soak so the sampler sees the clocks under this load
+        i = 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    clocks = clk.summary()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    vox_step = cfg.voxels * world
+    value = vox_step * args.steps / (ms * 1e-3)
+    if ww.device_error() != 0:
+        raise SystemExit("device error word set during the benchmark")
+
+    # ---- e2e through the public API from host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        L, R, w, b, out = sets[0]
+        hL = torch.empty(L.shape, dtype=L.dtype, pin_memory=True)
+        hR = torch.empty(R.shape, dtype=R.dtype, pin_memory=True)
+        hL.copy_(L)
+        hR.copy_(R)
+        hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        dL, dR = torch.empty_like(L), torch.empty_like(R)
+        e2e_steps = max(3, min(args.steps, 50))
+
+        def e2e_step():
+            dL.copy_(hL, non_blocking=True)
+            dR.copy_(hR, non_blocking=True)
+            ww.corr_cost_stem3d(dL, dR, w, b, cfg.D, cfg.G, act=cfg.act, out=out, stream=stream)
+            hout.copy_(out, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = f0.elapsed_time(f1)
+        if dist is not None:
+            t = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": vox_step * e2e_steps / (ems * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": (L.numel() + R.numel()) * L.element_size(),
+               "d2h_bytes_per_step": out.numel() * out.element_size(), "steps": e2e_steps}
+
+    # ---- roofline of the fused kernel (the only kernel in a step) ----
+    peaks = load_peaks()
+    t_launch = ms_per_step * 1e-3
+    tflops = cfg.stem_flops() / t_launch / 1e12
+    gbs = cfg.algorithmic_bytes() / t_launch / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get(cfg.name)
+    f_tc, f_hbm = tflops / peaks["tflops"], gbs / peaks["hbm_gbs"]
+    if f_tc >= f_hbm:
+        roof = {"bound": "tensor", "achieved": tflops, "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": f_tc}
+    else:
+        roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": f_hbm}
+    roof.update({"traffic": traffic, "peak_source": peaks["src"],
+                 "other": {"hbm_gbs": gbs, "hbm_frac": f_hbm, "tensor_tflops": tflops, "tensor_frac": f_tc}})
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        try:
+            cpu = cpu_baseline(cfg)
+        except Exception as e:  # the baseline never blocks the measurement
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {e}"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded normal/uniform features, N(0,0.05) weights)",
+        "config": {"workload": f"{cfg.name}: B={cfg.B} C={cfg.C} G={cfg.G} H={cfg.H} W={cfg.W} D={cfg.D} "
+                               f"Cout={cfg.Cout} fp16", "global_batch": cfg.B * world,
+                   "parallelism": f"batch-sharded replicas x{world} (no collective in the op)",
+                   "l2": f"{n_sets} rotating input/output sets, {n_sets * per_set / 2**20:.0f} MB > 126 MB L2"},
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

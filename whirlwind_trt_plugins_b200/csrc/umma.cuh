@@ -14,7 +14,7 @@
 //     conv taps are expressed without any im2col copy.
 //   * TMEM addresses are (lane << 16) | column.  Warp w of a warpgroup may
 //     only touch lanes [32*(w%4), 32*(w%4)+32).
-//   * Every wait is bounded (kSpinLimit polls); on expiry it returns false
+//   * Every wait is bounded (kWaitRounds suspended polls); on expiry it returns false
 //     and the caller records an error and winds down instead of hanging.
 #pragma once
 
@@ -24,9 +24,6 @@
 namespace ww {
 namespace umma {
 
-// Polls of an mbarrier before a wait is declared failed (~seconds at the
-// poll rate with backoff; far above any legitimate wait in these kernels).
-constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p)
 {
@@ -70,7 +67,9 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N)
 // MMA issue (one thread) and completion tracking
 // ---------------------------------------------------------------------------
 
-// D[tmem] (+)= A[smem] * B[smem]^T, one K=16 step.
+// D[tmem] (+)= A[smem] * B[smem]^T, one K=16 step.  No "memory" clobber:
+// operand visibility is ordered by fences + mbarriers, and leaving ordinary
+// loads free to move lets the compiler prefetch the next descriptors.
 __device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                            uint32_t idesc, uint32_t accumulate)
 {
@@ -79,8 +78,7 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
         :
-        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive (once) on an mbarrier when every MMA issued so far by this thread
@@ -222,13 +220,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t saddr, uint32_t parity)
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// nanoseconds (it resumes as soon as the phase completes), so waiting warps
+// do not spin through issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t saddr, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(saddr), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete: at most
+// kWaitRounds suspended polls of <= 1 ms each (seconds in total, orders of
+// magnitude above any legitimate wait in these kernels).
+constexpr uint32_t kWaitRounds = 4000;
 __device__ __forceinline__ bool mbar_wait(uint32_t saddr, uint32_t parity)
 {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(saddr, parity)) return true;
-        if (i > 64) __nanosleep(i > 4096 ? 256 : 32);
-    }
+    for (uint32_t i = 0; i < kWaitRounds; ++i)
+        if (mbar_try_wait_hint(saddr, parity, 1000000u)) return true;
     return false;
 }
 
@@ -245,6 +260,42 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_saddr, const void* src, ui
         :
         : "r"(dst_saddr), "l"(src), "r"(bytes), "r"(mbar_saddr)
         : "memory");
+}
+
+}  // namespace umma
+}  // namespace ww
+
+namespace ww {
+namespace umma {
+
+// 3-D tiled TMA load global -> shared, completion counted on an mbarrier.
+// `tmap` is the generic address of a CUtensorMap kernel parameter.
+// Coordinates are element indices (x innermost); x * sizeof(elem) must be a
+// multiple of 16 bytes; out-of-range elements are filled with zeros.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst_saddr, const void* tmap, int x, int y, int z,
+                                            uint32_t mbar_saddr)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];\n"
+        :
+        : "r"(dst_saddr), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(mbar_saddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap)
+{
+    asm volatile("prefetch.tensormap [%0];\n" : : "l"(tmap) : "memory");
+}
+
+// fp32 result of fp16 * fp16 + fp32 with a single rounding: identical to
+// fmaf((float)a, (float)b, c) because the product of two fp16 values is
+// exact in fp32.
+__device__ __forceinline__ float fma_f16f16f32(unsigned short a, unsigned short b, float c)
+{
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+    return d;
 }
 
 }  // namespace umma

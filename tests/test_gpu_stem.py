@@ -6,7 +6,9 @@
 * ww_cost_stem3d / ww_corr_cost_stem3d (tensor cores, fp32 accumulation in a
   different order than the oracle): |out - oracle| <= 2e-2 absolute (fp16
   tolerance of the north-star contract; values are already normalised by the
-  channel count in the correlation), with the volume itself bit-identical.
+  channel count in the correlation).  The fused kernel's correlation runs on
+  the tensor cores, so its volume can differ from CorrVolume's by one fp16
+  ulp in rare values.
 """
 import numpy as np
 import pytest
@@ -124,9 +126,12 @@ def test_fused_configs_match_oracle(ww, torch, orc, cfg_id):
     assert err <= ATOL_F16, f"max abs err {err}"
 
 
-def test_fused_equals_unfused_composition(ww, torch, orc):
-    """corr -> stem through HBM and the fused kernel give identical bits: the
-    fused volume is the CorrVolume result bit for bit."""
+def test_fused_matches_unfused_composition(ww, torch, orc):
+    """corr -> stem through HBM and the fused kernel agree: the fused kernel's
+    correlation runs on the tensor cores (its fp32 sums are added in another
+    order than CorrVolume's sequential fma chain), so a volume value may differ
+    by one fp16 ulp; the stem outputs stay within the fp16 tolerance and
+    almost all are bit-identical."""
     from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
     cfg = CONFIGS[2].scaled(H=9, W=40)
     x = make_inputs(cfg)
@@ -134,9 +139,32 @@ def test_fused_equals_unfused_composition(ww, torch, orc):
     fused = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
     vol = ww.corr_volume(tl, tr, cfg.D, cfg.G)
     unfused = ww.cost_stem3d(vol, tw, tb)
-    assert torch.equal(fused.view(torch.int16), unfused.view(torch.int16))
+    diff = (fused.float() - unfused.float()).abs()
+    assert float(diff.max()) <= ATOL_F16
+    assert float((diff == 0).float().mean()) >= 0.99
     ref_vol = orc.corr_f16(x["left"], x["right"], cfg.D, cfg.G)
     assert np.array_equal(_u16(vol.cpu().numpy()), _u16(ref_vol))
+
+
+@pytest.mark.parametrize("shape", [
+    # (B, C, G, H, W, D, Cout): channel widths on every correlation path
+    (1, 64, 2, 5, 24, 24, 16),     # Cg = 32: channels in two tensor-core chunks
+    (1, 40, 2, 4, 20, 20, 8),      # Cg = 20 (zero-padded chunk), W % 8 != 0 (scalar staging)
+    (2, 24, 8, 6, 33, 13, 32),     # Cg = 3, odd W and D
+    (1, 16, 16, 3, 16, 70, 16),    # Cg = 1, five M-blocks along D
+    (1, 96, 8, 4, 24, 64, 16),     # Cg = 12 (m16n8k16 with padded channels)
+    (1, 48, 3, 5, 16, 9, 4),       # lone octet with 3 groups, D < 16
+])
+def test_fused_shapes_match_oracle(ww, torch, orc, shape):
+    from whirlwind_trt_plugins_b200.configs import FrontEnd, make_inputs
+    B, C, G, H, W, D, Cout = shape
+    cfg = FrontEnd("edge", B=B, C=C, G=G, H=H, W=W, D=D, Cout=Cout)
+    x = make_inputs(cfg, seed=C + W + D)
+    out = _fused(ww, torch, x, cfg).cpu().numpy().astype(np.float32)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=orc.ACC_F64)
+    err = np.abs(out - ref.astype(np.float32)).max()
+    assert err <= ATOL_F16, f"max abs err {err}"
+    assert ww.device_error() == 0
 
 
 @pytest.mark.parametrize("cfg_id", [2, 5])

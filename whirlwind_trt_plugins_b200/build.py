@@ -32,6 +32,7 @@ SOURCES = [
     "corr_volume.cu",
     "cost_stem3d_ref3.cu",
     "stem_tc.cu",
+    "tensor_map.cu",
     "plugin_core.cpp",
 ]
 TRT_SOURCES = ["trt/ww_trt_plugins.cpp"]

@@ -15,12 +15,14 @@
 //
 //   loader (1 warp)     stages, per group octet ("job"), the left columns
 //                       [w0-8, w0+16) and right columns [w0-8*ceil(D/8), w0+16)
-//                       of the octet's channels into a two-slot ring with one
-//                       1-D bulk copy (TMA engine) per channel row and side;
-//                       completion is counted in bytes on an mbarrier.
-//   producers (8 warps) compute the octet's correlation (fused; bit-identical
-//                       to the CorrVolume kernels) or gather it (volume mode)
-//                       into the volume buffer in the UMMA K-major layout
+//                       of the octet's channels into a ring of 2..4 slots with
+//                       16-byte cp.async copies (zero fill outside the image);
+//                       completion is counted on an mbarrier.
+//   producers (8 warps) compute the octet's correlation (fused mode) on the
+//                       warp-level tensor cores (mma.sync, fp32 accumulation;
+//                       see corr_task_mma) or gather it from a volume tensor
+//                       (volume mode) into the volume buffer in the UMMA
+//                       K-major layout
 //                           [group octet][d' = d+1][w' = w-w0+1][8 groups x fp16]
 //   MMA (1 warp)        for each 128-voxel M-block (16 disparities x 8 columns)
 //                       and K-step (two 8-group octets of one or two (kd, kw)
@@ -47,8 +49,8 @@
 // memory, so the issue path does not queue behind the producers' loads.
 //
 // Synchronisation (mbarriers, every wait bounded):
-//   stage_full[2]   loader (bulk-copy bytes) -> producers
-//   stage_empty[2]  producers -> loader
+//   stage_full[ns]  loader (cp.async completion) -> producers
+//   stage_empty[ns] producers (one arrival per task) -> loader
 //   vol_full[2]     producers -> MMA        volume buffer ready
 //   vol_empty[2]    MMA (commit) -> producers   all MMAs reading it finished
 //   acc_full[m]     MMA (commit) -> epilogue    row u-1 of M-block m complete
@@ -57,6 +59,7 @@
 // waiting role stops, the others run into their own bounded waits, and the
 // CTA winds down and frees its tensor memory.
 
+#include "tensor_map.cuh"
 #include "umma.cuh"
 #include "ww_common.cuh"
 
@@ -80,6 +83,7 @@ constexpr int kProdWarps = 8;
 constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;  // 448
 constexpr int kMaxMB = 10;         // M-blocks per CTA (TMEM: kMaxMB * 3 * 16 <= 512)
 constexpr int kLStageW = 24;       // staged left columns [w0-8, w0+16)
+constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 4;       // staging ring depth
 
@@ -99,12 +103,25 @@ struct StemParams {
     int vec_ok;
     int rstage_w;             // staged right columns
     int n_slots;              // staging ring depth (2..kMaxSlots)
+    int n_tiles;              // 8-column right tiles per job: ceil(D/8) + 2
+    int tpj;                  // producer tasks per job (each a range of right tiles)
+    int raw_w_smem;           // 1: weights are staged through shared memory at set-up
+    int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
+    int n_rbox;               // right boxes of 64 columns per job
     uint32_t tmem_cols;
-    uint32_t off_b, off_vol, vol_buf_bytes, lbo_vol, off_stage, stage_slot_bytes, stage_group_bytes, off_bar;
+    uint32_t off_b, off_vol, vol_buf_bytes, lbo_vol, off_stage, stage_slot_bytes, off_bar;
+    uint32_t rbox_bytes;      // one right box: 8 Cg rows x 128 bytes
+    uint32_t off_l;           // left rows within a slot
+    uint32_t stage_tx;        // bytes a job's TMA copies deliver
+    uint32_t off_zero;        // 128 zero bytes (rows of absent channels)
     // Per K-step descriptor templates with a zero base address: A relative to a
     // volume buffer, B relative to the B image.  Read with uniform loads.
     uint64_t tmplA[kMaxSteps];
     uint64_t tmplB[kMaxSteps];
+    // TMA maps of the left / right features (4-D: x = W, y = row, z = channel,
+    // w = batch); boxes [24] x [8 Cg] (left) and [64] x [8 Cg] (right, swizzled).
+    CUtensorMap tmap_l;
+    CUtensorMap tmap_r;
 };
 
 // K-step s -> (tap, group octet) of its two 8-channel core matrices.
@@ -176,34 +193,178 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* er
     return __all_sync(0xffffffffu, ok);
 }
 
-// Correlation of one group for a 2-column x 8-disparity tile:
-//   acc[h][dd] = sum_c L[c][x0 + h] * R[c][x0 + h - dd]   (staged coordinates)
-// as one fp32 fma chain per output in channel order (bit-identical to the
-// reference).  lp -> L[0][x0] (left rows of kLStageW), rp -> R[0][x0 - 7]
-// (right rows of rw, 4-byte aligned).  CG > 0: compile-time channel count,
-// fully unrolled so every load is issued ahead of its FMAs; CG == 0: runtime.
-template <int CG>
-__device__ __forceinline__ void corr_tile(const unsigned short* __restrict__ lp, const __half* __restrict__ rp,
-                                          int rw, int cg_rt, float (&acc)[2][8])
+// Scale, round and store one 16x8 tile of correlation accumulators (8 groups
+// per slot) into the volume buffer vsa ([d' = d+1][w'][8 groups] rows).
+// Accumulator slot s of thread t is row m + 8 (s >> 1) (volume column
+// w' = m + 8 (s >> 1)), column 2q + (s & 1) of right tile jt (staged right
+// index 8 jt + 2q + (s & 1)), i.e. disparity d = 8 ceil(D/8) - 1 + w' - index.
+__device__ __forceinline__ void store_corr_tile(const StemParams& p, const float (&acc)[8][4], uint32_t vsa,
+                                                int jt, int lane)
 {
-    const int cg = CG > 0 ? CG : cg_rt;
+    const int m = lane >> 2, q = lane & 3;
+    const int dbase = 8 * (p.n_tiles - 2) - 1;
+    const bool div = p.scale_div != 0;
+    const float inv_cg = p.inv_cg, cgf = static_cast<float>(p.Cg);
 #pragma unroll
-    for (int cc = 0; cc < cg; ++cc) {
-        const unsigned short l0 = lp[cc * kLStageW];
-        const unsigned short l1 = lp[cc * kLStageW + 1];
-        const uint32_t* rq = reinterpret_cast<const uint32_t*>(rp + cc * rw);
-        unsigned short r[10];
+    for (int s = 0; s < 4; ++s) {
+        const int wp = m + 8 * (s >> 1);
+        const int d = dbase + wp - (8 * jt + 2 * q + (s & 1));
+        if (wp < kWtp && d >= 0 && d < p.D) {
+            uint32_t h[4];
 #pragma unroll
-        for (int q = 0; q < 5; ++q) {
-            const uint32_t x = rq[q];
-            r[2 * q] = static_cast<unsigned short>(x & 0xffffu);
-            r[2 * q + 1] = static_cast<unsigned short>(x >> 16);
+            for (int k = 0; k < 4; ++k) {
+                const float v0 = div ? __fdiv_rn(acc[2 * k][s], cgf) : __fmul_rn(acc[2 * k][s], inv_cg);
+                const float v1 = div ? __fdiv_rn(acc[2 * k + 1][s], cgf) : __fmul_rn(acc[2 * k + 1][s], inv_cg);
+                const __half2 h2 = __floats2half2_rn(v0, v1);
+                h[k] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            st_shared_v4(vsa + static_cast<uint32_t>(((d + 1) * kWtp + wp) * 16), h[0], h[1], h[2], h[3]);
         }
+    }
+}
+
+// Staged layout of one job (slot base 1024-byte aligned; row r = e * Cg + c
+// is channel c of group e of the octet):
+//   right: n_rbox boxes of [8 Cg rows][64 fp16] (128-byte rows, 128-byte TMA
+//          swizzle: 16-byte chunk j of row r sits at chunk j ^ (r & 7)), box k
+//          holding staged right columns [64 k, 64 k + 64) = image columns
+//          w0 - 8 ceil(D/8) + 64 k + ...
+//   left:  at off_l, [8 Cg rows][24 fp16] (48-byte rows), image columns
+//          w0 - 8 .. w0 + 15.
+// Address of the 16-byte right chunk holding staged columns [8 jt, 8 jt + 8)
+// of row r, given rb = slot + r * 128:
+__device__ __forceinline__ uint32_t rchunk(uint32_t rb, int r, int jt, uint32_t rbox_bytes)
+{
+    return rb + static_cast<uint32_t>(jt >> 3) * rbox_bytes + ((static_cast<uint32_t>((jt & 7) ^ (r & 7))) << 4);
+}
+
+// Group-wise correlation of one staging job (the 8 groups of a group octet,
+// one volume row) for right-column tiles [jt0, jt1), on the warp-level
+// tensor cores.  Per group the band is a small GEMM
+//     P[x][x'] = sum_c L[c][x] * R[c][x']          vol[d][x] = P[x][x - d] / Cg
+// with M = the 10 volume columns x (w' = 0..9, padded to 16 rows), K = the
+// group's channels and N = 8 staged right columns x'.  Thread t of the warp
+// holds the same four (x, x') accumulator slots for every group of the
+// octet, so each slot it owns becomes one 16-byte row of the volume buffer
+// (8 groups of one (d, w') position) written with a single vector store.
+// Products of fp16 values are exact in fp32; the tensor core adds the Cg
+// products in its own order, so a volume value can differ from the CorrVolume
+// kernels' sequential fp32 fma chain in the last fp32 bits (and, rarely, by
+// one fp16 ulp after rounding).
+// KM = 8: Cg <= 8 (m16n8k8); KM = 16: 8 < Cg <= 16 (m16n8k16).  Channels
+// >= Cg read zeros (A: predicated loads; B: a zeroed 128-byte row).
+template <int KM>
+__device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
+                                              uint32_t vsa, int jt0, int jt1, int lane)
+{
+    constexpr int NA = KM == 8 ? 2 : 4;  // A registers per group
+    constexpr int NB = KM == 8 ? 1 : 2;  // B registers per group and tile
+    constexpr int NI = KM == 8 ? 2 : 4;  // ldmatrix.x4 per tile
+    const int m = lane >> 2, q = lane & 3;
+    const int Cg = p.Cg;
+    const uint32_t lslot = slot + p.off_l;
+
+    // A fragments: rows m (w' = m) and m + 8 (w' = m + 8) of the left block;
+    // the staged left index of w' is w' + 7.
+    uint32_t a[8][NA];
 #pragma unroll
-        for (int dd = 0; dd < 8; ++dd) {
-            acc[0][dd] = fma_f16f16f32(l0, r[7 - dd], acc[0][dd]);
-            acc[1][dd] = fma_f16f16f32(l1, r[8 - dd], acc[1][dd]);
+    for (int e = 0; e < 8; ++e) {
+#pragma unroll
+        for (int r = 0; r < NA; ++r) {
+            const int c0 = 2 * q + 8 * (r >> 1);
+            const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * (m + 7 + 8 * (r & 1)));
+            const unsigned short lo = c0 < Cg ? ld_shared_u16(la) : 0;
+            const unsigned short hi = c0 + 1 < Cg ? ld_shared_u16(la + kLRowBytes) : 0;
+            a[e][r] = pack_b16x2(lo, hi);
         }
+    }
+
+    // ldmatrix row of this lane: matrix i = lane / 8 is (group, k-half), its
+    // row lane % 8 a channel.
+    const int mi = lane >> 3, rr = lane & 7;
+    uint32_t rb[NI];
+    int rrow[NI];
+#pragma unroll
+    for (int k = 0; k < NI; ++k) {
+        const int e = KM == 8 ? 4 * k + mi : 2 * k + (mi >> 1);
+        const int c = KM == 8 ? rr : 8 * (mi & 1) + rr;
+        rrow[k] = c < Cg ? e * Cg + c : -1;
+        rb[k] = rrow[k] >= 0 ? slot + static_cast<uint32_t>(rrow[k]) * 128u : zero_row;
+    }
+
+    for (int jt = jt0; jt < jt1; ++jt) {
+        __syncwarp();
+        uint32_t b[8][NB];
+#pragma unroll
+        for (int k = 0; k < NI; ++k) {
+            uint32_t r4[4];
+            const uint32_t addr = rrow[k] >= 0 ? rchunk(rb[k], rrow[k], jt, p.rbox_bytes)
+                                               : rb[k] + (static_cast<uint32_t>(jt & 7) << 4);
+            ldmatrix_x4_trans(addr, r4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (KM == 8) b[4 * k + i][0] = r4[i];
+                else b[2 * k + (i >> 1)][i & 1] = r4[i];
+            }
+        }
+        float acc[8][4];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+#pragma unroll
+            for (int s = 0; s < 4; ++s) acc[e][s] = 0.0f;
+            if (KM == 8) mma_16x8x8_f16f32(acc[e], a[e][0], a[e][1], b[e][0]);
+            else mma_16x8x16_f16f32(acc[e], a[e][0], a[e][1], a[e][2], a[e][3], b[e][0], b[e][NB - 1]);
+        }
+        store_corr_tile(p, acc, vsa, jt, lane);
+    }
+}
+
+// Cg > 16: the channels run through the tensor core in chunks of 16 (the
+// last one zero-padded), with the fragments of each chunk loaded per tile.
+__device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t slot, uint32_t zero_row,
+                                                   uint32_t vsa, int jt0, int jt1, int lane)
+{
+    const int m = lane >> 2, q = lane & 3;
+    const int mi = lane >> 3, rr = lane & 7;
+    const int Cg = p.Cg;
+    const uint32_t lslot = slot + p.off_l;
+    for (int jt = jt0; jt < jt1; ++jt) {
+        float acc[8][4];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int s = 0; s < 4; ++s) acc[e][s] = 0.0f;
+        for (int kc = 0; kc < Cg; kc += 16) {
+            __syncwarp();
+            uint32_t b[8][2];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int e = 2 * k + (mi >> 1);
+                const int c = kc + 8 * (mi & 1) + rr;
+                const int r = e * Cg + c;
+                uint32_t r4[4];
+                ldmatrix_x4_trans(c < Cg ? rchunk(slot + static_cast<uint32_t>(r) * 128u, r, jt, p.rbox_bytes)
+                                         : zero_row + (static_cast<uint32_t>(jt & 7) << 4),
+                                  r4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) b[2 * k + (i >> 1)][i & 1] = r4[i];
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                uint32_t a[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int c0 = kc + 2 * q + 8 * (r >> 1);
+                    const uint32_t la =
+                        lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * (m + 7 + 8 * (r & 1)));
+                    const unsigned short lo = c0 < Cg ? ld_shared_u16(la) : 0;
+                    const unsigned short hi = c0 + 1 < Cg ? ld_shared_u16(la + kLRowBytes) : 0;
+                    a[r] = pack_b16x2(lo, hi);
+                }
+                mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
+            }
+        }
+        store_corr_tile(p, acc, vsa, jt, lane);
     }
 }
 
@@ -252,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             mbar_init(smem_addr(&vol_empty[i]), 1);
         }
         for (int i = 0; i < p.n_slots; ++i) {
-            mbar_init(smem_addr(&stage_full[i]), 32);
+            mbar_init(smem_addr(&stage_full[i]), p.use_tma ? 1 : 32);
             mbar_init(smem_addr(&stage_empty[i]), kProdWarps);
         }
         mbar_init(smem_addr(final_bar), 1);
@@ -264,6 +425,23 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     }
     if (warp == kMmaWarp) tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
 
+    // Weights [Cout][G][27] fp16.  When aligned, they are first copied into
+    // shared memory (the volume and staging regions, unused until set-up
+    // ends) with coalesced 16-byte copies; the B image is then gathered from
+    // there instead of with scattered 2-byte global loads.
+    const __half* wsrc = p.w;
+    if (p.raw_w_smem) {
+        const uint32_t wbytes = static_cast<uint32_t>(p.Cout * p.G * 54);
+        const uint32_t dst0 = smem_addr(sVol);
+        for (uint32_t i = threadIdx.x * 16; i < wbytes; i += kThreads * 16)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n"
+                         :
+                         : "r"(dst0 + i), "l"(reinterpret_cast<const uint8_t*>(p.w) + i)
+                         : "memory");
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        __syncthreads();
+        wsrc = reinterpret_cast<const __half*>(sVol);
+    }
     // B image: step s, chunk c, row n (= blk*COUTP + o), 8 fp16 of consecutive groups.
     for (int i = threadIdx.x; i < p.nsteps * 2 * NR; i += kThreads) {
         const int n = i % NR;
@@ -278,18 +456,22 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int g = kg * 8 + e;
-            float x = 0.0f;
+            __half x = __float2half_rn(0.0f);
             if (tap >= 0 && o < p.Cout && g < p.G) {
                 const int kd = tap / 3, kw = tap - 3 * (tap / 3);
-                x = __half2float(p.w[(i64(o) * p.G + g) * 27 + kd * 9 + kh * 3 + kw]);
+                x = wsrc[(i64(o) * p.G + g) * 27 + kd * 9 + kh * 3 + kw];
             }
-            v[e] = __float2half_rn(x);
+            v[e] = x;
         }
         *reinterpret_cast<uint4*>(sB + static_cast<size_t>(i) * 16) = *reinterpret_cast<uint4*>(v);
     }
-    // Both volume buffers start as zeros: halo planes and padding stay zero.
+    __syncthreads();  // the staged weights are consumed before the region is zeroed
+    // Both volume buffers start as zeros: halo planes and padding stay zero;
+    // so do the zero rows that stand in for absent channels.
     for (uint32_t i = threadIdx.x * 16; i < 2 * p.vol_buf_bytes; i += kThreads * 16)
         *reinterpret_cast<uint4*>(sVol + i) = make_uint4(0, 0, 0, 0);
+    for (uint32_t i = threadIdx.x * 16; i < 128u; i += kThreads * 16)
+        *reinterpret_cast<uint4*>(smem + p.off_zero + i) = make_uint4(0, 0, 0, 0);
 
     fence_proxy_async_smem();
     fence_before_sync();
@@ -446,84 +628,93 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         }
     } else if (warp == kLoadWarp) {
         // ======================= loader =======================
-        // Job j = (volume row uv0 + j / KG, group octet j % KG) -> slot j % NS.
-        // Per group: left [Cg][24] then right [Cg][rstage_w] fp16, regions
-        // padded so consecutive groups start 16 bytes apart modulo 128.  Lanes
-        // take whole channel rows and cp.async them in 16-byte vectors (zero
-        // fill outside the image); each lane's copies complete onto stage_full.
+        // Job j = (volume row uv0 + j / KG, group octet j % KG) -> slot j % NS,
+        // in the layout described at rchunk().  With TMA: one elected lane
+        // arms stage_full with the job's byte count and issues n_rbox + 1 box
+        // copies (zero fill outside the image and past the last channel).
+        // Otherwise (W % 8 != 0 or unaligned features) lanes copy 16-byte
+        // vectors of whole channel rows with cp.async (or element by element).
         if (FUSED) {
             const int Cg = p.Cg;
-            const int rw = p.rstage_w;
             const int NS = p.n_slots;
             const int n_runs = (p.D + 7) / 8;
             const int rbase = w0 - 8 * n_runs;
-            const int nvr = rw / 8;
+            const int nvr = p.rstage_w / 8;
             int issued = 0;
             for (int j = 0; j < total_jobs; ++j) {
                 const int slot = j % NS;
                 if (j >= NS && !warp_wait(smem_addr(&stage_empty[slot]), ((j / NS) - 1) & 1, p.err, 6)) break;
                 issued = j + 1;
-                uint8_t* sbase = smem + p.off_stage + slot * p.stage_slot_bytes;
+                const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
                 const int urow = uv0 + j / p.KG - p.in_row0;
                 const int kg = j % p.KG;
-                for (int lc = lane; lc < 8 * Cg; lc += 32) {
+                const uint32_t full = smem_addr(&stage_full[slot]);
+                if (p.use_tma) {
+                    if (elect_one()) {
+                        mbar_arrive_expect_tx(full, p.stage_tx);
+                        for (int k = 0; k < p.n_rbox; ++k)
+                            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, rbase + 64 * k, urow, kg * 8 * Cg, b,
+                                        full);
+                        tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, kg * 8 * Cg, b, full);
+                    }
+                    __syncwarp();
+                    continue;
+                }
+                for (int lc = lane; lc < 8 * Cg; lc += 32) {  // lc = row of the job (e * Cg + c)
                     const int ge = lc / Cg, cc = lc - ge * Cg;
                     const int g = kg * 8 + ge;
                     const bool gv = g < p.G;
                     const int64_t roff = ((i64(b) * p.C + (gv ? g * Cg + cc : 0)) * p.in_rows + urow) * p.W;
-                    uint8_t* gdst = sbase + ge * p.stage_group_bytes;
                     for (int v = 0; v < 3 + nvr; ++v) {
                         const bool isL = v < 3;
                         const int x = isL ? (w0 - 8 + 8 * v) : (rbase + 8 * (v - 3));
-                        uint8_t* dst = gdst + (isL ? cc * (kLStageW * 2) + 16 * v
-                                                   : Cg * (kLStageW * 2) + cc * rw * 2 + 16 * (v - 3));
+                        const uint32_t dst = isL ? sbase + p.off_l + lc * kLRowBytes + 16 * v
+                                                 : rchunk(sbase + lc * 128u, lc, v - 3, p.rbox_bytes);
                         const __half* srow = (isL ? p.left : p.right) + roff;
                         if (p.vec_ok) {
                             const bool in = gv && x >= 0 && x < p.W;  // whole vector (W % 8 == 0)
                             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
                                          :
-                                         : "r"(smem_addr(dst)), "l"(in ? srow + x : srow), "r"(in ? 16 : 0)
+                                         : "r"(dst), "l"(in ? srow + x : srow), "r"(in ? 16 : 0)
                                          : "memory");
                         } else {
-                            __half* d16 = reinterpret_cast<__half*>(dst);
+                            __align__(16) __half h[8];
 #pragma unroll
                             for (int q = 0; q < 8; ++q) {
                                 const int xx = x + q;
-                                d16[q] = (gv && xx >= 0 && xx < p.W) ? srow[xx] : __float2half_rn(0.0f);
+                                h[q] = (gv && xx >= 0 && xx < p.W) ? srow[xx] : __float2half_rn(0.0f);
                             }
+                            const uint4 v4 = *reinterpret_cast<const uint4*>(h);
+                            st_shared_v4(dst, v4.x, v4.y, v4.z, v4.w);
                         }
                     }
                 }
                 if (p.vec_ok) {
-                    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n"
-                                 :
-                                 : "r"(smem_addr(&stage_full[slot]))
-                                 : "memory");
+                    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" : : "r"(full) : "memory");
                 } else {
                     __threadfence_block();
-                    mbar_arrive(smem_addr(&stage_full[slot]));
+                    mbar_arrive(full);
                 }
             }
-            // Nothing may still be landing in shared memory when the CTA exits.
+            // Nothing may still be landing in shared memory when the CTA exits:
+            // wait (bounded) for the last fill of each slot, then for any
+            // cp.async of this thread.
+            for (int j = std::max(0, issued - NS); j < issued; ++j)
+                wait_or_fail(smem_addr(&stage_full[j % NS]), (j / NS) & 1, p.err, 8);
             asm volatile("cp.async.wait_all;\n" ::: "memory");
-            (void)issued;
         }
     } else {
         // ======================= producers =======================
-        // Fused mode: lane (e = lane/4, pp = lane%4) of a producer warp computes
-        // group e's correlation for a 2-column x 8-disparity tile of the job's
-        // octet; stmatrix.trans then writes the eight groups of each position
-        // as one 16-byte row of the volume buffer.  Warps run independently,
-        // synchronised only through the stage and volume mbarriers.
+        // Fused mode: the job of each (volume row, group octet) is split into
+        // tpj tasks (ranges of right-column tiles); task tau = job * tpj + h
+        // goes to producer warp tau mod kProdWarps, which runs the
+        // tensor-core correlation of corr_task_mma on it.  Every warp waits on
+        // and releases every job (and every volume row) in order, with or
+        // without tasks in it, so no warp's parity wait can fall two phases
+        // behind a barrier.  Volume mode: the warps gather the row's slice of
+        // the volume tensor.
         const int pw = warp - kProdWarp0;
-        const int e = lane >> 2;
-        const int pp = lane & 3;
-        const int Cg = p.Cg;
-        const int rw = p.rstage_w;
-        const int n_runs = (p.D + 7) / 8;
-        const int n_tasks = n_runs + (n_runs + 3) / 4;
-        const float cgf = static_cast<float>(Cg);
-        int job = 0;
+        const uint32_t zero_row = smem_addr(smem + p.off_zero);
         bool ok = true;
         for (int it = 0; it < n_iter && ok; ++it) {
             const int u = u_first + it;
@@ -531,88 +722,30 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             if (it >= 2 && !warp_wait(smem_addr(&vol_empty[vb]), ((it - 2) >> 1) & 1, p.err, 4)) break;
             if (u >= 0 && u < p.H) {
                 uint8_t* vbuf = sVol + vb * p.vol_buf_bytes;
-                for (int kg = 0; kg < p.KG; ++kg) {
-                    if (FUSED) {
+                if (FUSED) {
+                    const int job0 = (u - uv0) * p.KG;  // job of (u, octet 0)
+                    for (int kg = 0; kg < p.KG && ok; ++kg) {
+                        const int job = job0 + kg;
                         const int slot = job % p.n_slots;
-                        if (!warp_wait(smem_addr(&stage_full[slot]), (job / p.n_slots) & 1, p.err, 7)) { ok = false; break; }
-                        const uint8_t* gbase = smem + p.off_stage + slot * p.stage_slot_bytes + e * p.stage_group_bytes;
-                        const unsigned short* Ls = reinterpret_cast<const unsigned short*>(gbase);
-                        const __half* Rs = reinterpret_cast<const __half*>(gbase + Cg * (kLStageW * 2));
+                        if (!warp_wait(smem_addr(&stage_full[slot]), (job / p.n_slots) & 1, p.err, 7)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
                         const uint32_t vsa = smem_addr(vbuf + kg * p.lbo_vol);
-                        const int g = kg * 8 + e;
-                        for (int task = pw; task < n_tasks; task += kProdWarps) {
-                            const bool nice = task < n_runs;          // columns 0..7, one disparity run
-                            const int pr = nice ? pp : 4;              // column pair
-                            const int run = nice ? task : 4 * (task - n_runs) + pp;
-                            const bool active = run < n_runs && g < p.G;
-                            float acc[2][8];
-#pragma unroll
-                            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                                for (int dd = 0; dd < 8; ++dd) acc[h][dd] = 0.0f;
-                            if (active) {
-                                const unsigned short* lp = Ls + 2 * pr + 7;
-                                const __half* rp = Rs + 2 * pr - 8 * run - 8 + 8 * n_runs;
-                                switch (Cg) {  // fully unrolled for the common group widths
-                                    case 4: corr_tile<4>(lp, rp, rw, Cg, acc); break;
-                                    case 8: corr_tile<8>(lp, rp, rw, Cg, acc); break;
-                                    case 12: corr_tile<12>(lp, rp, rw, Cg, acc); break;
-                                    case 16: corr_tile<16>(lp, rp, rw, Cg, acc); break;
-                                    default: corr_tile<0>(lp, rp, rw, Cg, acc); break;
-                                }
-                            }
-                            // fp16 values, packed (h = 0 low, h = 1 high) per disparity
-                            uint32_t packed[8];
-                            const int wa0 = w0 - 1 + 2 * pr;
-                            const bool interior = active && wa0 >= 0 && wa0 + 1 < p.W && 8 * run + 7 < p.D &&
-                                                  wa0 - (8 * run + 7) >= 0;
-                            if (interior && !p.scale_div) {
-#pragma unroll
-                                for (int dd = 0; dd < 8; ++dd) {
-                                    const __half2 h2 = __floats2half2_rn(__fmul_rn(acc[0][dd], p.inv_cg),
-                                                                         __fmul_rn(acc[1][dd], p.inv_cg));
-                                    packed[dd] = *reinterpret_cast<const uint32_t*>(&h2);
-                                }
-                            } else {
-#pragma unroll
-                                for (int dd = 0; dd < 8; ++dd) {
-                                    const int d = 8 * run + dd;
-                                    uint32_t hv[2];
-#pragma unroll
-                                    for (int h = 0; h < 2; ++h) {
-                                        const int wa = wa0 + h;
-                                        float v = 0.0f;
-                                        if (active && wa >= 0 && wa < p.W && d < p.D && wa - d >= 0)
-                                            v = p.scale_div ? __fdiv_rn(acc[h][dd], cgf) : __fmul_rn(acc[h][dd], p.inv_cg);
-                                        hv[h] = __half_as_ushort(__float2half_rn(v));
-                                    }
-                                    packed[dd] = hv[0] | (hv[1] << 16);
-                                }
-                            }
-                            // Row address this lane supplies: matrix mi = lane/8, row rr = lane%8
-                            // -> position of lane-group pp' = rr/2, column h = rr%2, disparity 4s+mi.
-                            const int mi = lane >> 3, rr = lane & 7;
-                            const int pq = rr >> 1, hq = rr & 1;
-                            const int prq = nice ? pq : 4;
-                            const int runq = nice ? task : 4 * (task - n_runs) + pq;
-#pragma unroll
-                            for (int sg = 0; sg < 2; ++sg) {
-                                const int dq = 8 * runq + 4 * sg + mi;
-                                int pos;
-                                if (runq < n_runs) pos = (dq + 1) * kWtp + 2 * prq + hq;
-                                else pos = (Dtp - 1) * kWtp + hq;  // inactive: an always-zero plane, zeros written
-                                asm volatile(
-                                    "stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};\n"
-                                    :
-                                    : "r"(vsa + pos * 16), "r"(packed[4 * sg + 0]), "r"(packed[4 * sg + 1]),
-                                      "r"(packed[4 * sg + 2]), "r"(packed[4 * sg + 3])
-                                    : "memory");
-                            }
+                        // this warp's tasks of the job: tau = job * tpj + h, tau % kProdWarps == pw
+                        for (int h = ((pw - job * p.tpj) % kProdWarps + kProdWarps) % kProdWarps; h < p.tpj;
+                             h += kProdWarps) {
+                            const int jt0 = (h * p.n_tiles) / p.tpj, jt1 = ((h + 1) * p.n_tiles) / p.tpj;
+                            if (p.Cg <= 8) corr_task_mma<8>(p, sbase, zero_row, vsa, jt0, jt1, lane);
+                            else if (p.Cg <= 16) corr_task_mma<16>(p, sbase, zero_row, vsa, jt0, jt1, lane);
+                            else corr_task_mma_wide(p, sbase, zero_row, vsa, jt0, jt1, lane);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
-                        ++job;
-                    } else {
+                    }
+                } else {
+                    for (int kg = 0; kg < p.KG; ++kg) {
                         // Volume mode: gather vol[b, g, d, u, w] into the octet's rows.
                         const int64_t plane = i64(p.H) * p.W;
                         for (int i = pw * 32 + lane; i < 8 * p.D * kWtp; i += kProdWarps * 32) {
@@ -715,7 +848,8 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.rstage_w = 16 + 8 * ((D + 7) / 8);  // right columns [w0 - 8*ceil(D/8), w0 + 16)
     p.tmem_cols = pow2_cols(static_cast<uint32_t>(n_mb * 3 * coutp));
 
-    // shared-memory layout
+    // shared-memory layout: B image | 2 volume buffers | zero row, barriers |
+    // staging ring (1024-byte aligned slots for the 128-byte TMA swizzle)
     uint32_t off = 0;
     p.off_b = off;
     off += static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
@@ -727,23 +861,40 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.vol_buf_bytes = p.lbo_vol * KG + 128;
     off += 2 * p.vol_buf_bytes;
     off = (off + 127) & ~127u;
-    p.off_stage = off;
-    // Per group: left [Cg][24] then right [Cg][rstage_w] fp16, padded so that
-    // consecutive groups start 16 bytes apart modulo 128 (different banks).
-    p.stage_group_bytes = static_cast<uint32_t>(((Cg * (kLStageW + p.rstage_w) * 2 + 127) / 128) * 128 + 16);
-    p.stage_slot_bytes = fused ? ((8 * p.stage_group_bytes + 127) / 128) * 128 : 0;
+    p.off_zero = off;
+    off += 128;
     auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((5 + 2 * ns + 2 * n_mb) * 8 + 16); };
+    p.off_bar = off;
+    off += bar_bytes(kMaxSlots);
+    off = (off + 1023) & ~1023u;
+    p.off_stage = off;
+    p.n_tiles = (D + 7) / 8 + 2;
+    p.n_rbox = (p.rstage_w + 63) / 64;
+    p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
+    p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
+    p.stage_slot_bytes = fused ? ((p.off_l + 8u * Cg * kLRowBytes + 1023) / 1024) * 1024 : 0;
+    p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + kLStageW) * 8 * Cg * 2);
     // as many staging slots (2..kMaxSlots) as shared memory holds
     p.n_slots = 2;
-    while (p.n_slots < kMaxSlots && off + (p.n_slots + 1) * p.stage_slot_bytes + bar_bytes(p.n_slots + 1) <=
-                                        static_cast<uint32_t>(dev.smem_optin))
+    while (fused && p.n_slots < kMaxSlots &&
+           off + (p.n_slots + 1) * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin))
         ++p.n_slots;
-    off += p.n_slots * p.stage_slot_bytes;
-    off = (off + 127) & ~127u;
-    p.off_bar = off;
-    off += bar_bytes(p.n_slots);
+    off += fused ? p.n_slots * p.stage_slot_bytes : 0;
     const size_t smem = off;
     if (smem > static_cast<size_t>(dev.smem_optin)) return WW_ERR_UNSUPPORTED;
+    // Tasks per job: enough to give every producer warp work in each volume
+    // row, at most one per right tile.
+    p.tpj = std::min(p.n_tiles, std::max(1, (kProdWarps + KG - 1) / KG));
+    {
+        const size_t wbytes = static_cast<size_t>(Cout) * G * 54;
+        p.raw_w_smem = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0) &&
+                       (wbytes <= static_cast<size_t>(2 * p.vol_buf_bytes));
+    }
+    p.use_tma = 0;
+    if (fused && p.vec_ok && 8 * Cg <= 256) {
+        p.use_tma = encode_feature_map(&p.tmap_l, left, B, C, in_rows, W, kLStageW, 8 * Cg, false) &&
+                    encode_feature_map(&p.tmap_r, right, B, C, in_rows, W, 64, 8 * Cg, true);
+    }
 
     // Descriptor templates (base address 0; the kernel adds its buffer bases).
     for (int s = 0; s < nsteps; ++s) {

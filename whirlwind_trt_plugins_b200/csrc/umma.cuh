@@ -283,6 +283,19 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst_saddr, const void* tmap
         : "memory");
 }
 
+// 4-D tiled TMA load global -> shared (this CTA), completion counted on an
+// mbarrier; same coordinate rules as tma_load_3d.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst_saddr, const void* tmap, int x, int y, int z, int w,
+                                            uint32_t mbar_saddr)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5}], [%6];\n"
+        :
+        : "r"(dst_saddr), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(mbar_saddr)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap)
 {
     asm volatile("prefetch.tensormap [%0];\n" : : "l"(tmap) : "memory");
@@ -296,6 +309,57 @@ __device__ __forceinline__ float fma_f16f16f32(unsigned short a, unsigned short 
     float d;
     asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
     return d;
+}
+
+// ---- warp-level (mma.sync) helpers for small banded tiles ----
+
+__device__ __forceinline__ unsigned short ld_shared_u16(uint32_t saddr)
+{
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(saddr));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t pack_b16x2(unsigned short lo, unsigned short hi)
+{
+    uint32_t r;
+    asm("mov.b32 %0, {%1, %2};\n" : "=r"(r) : "h"(lo), "h"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" : : "r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+// Four 8x8 b16 matrices, transposed: lanes 8i..8i+7 give the row addresses
+// of matrix i; register i receives its fragment (thread t: rows 2(t%4) and
+// 2(t%4)+1 of column t/4).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(saddr));
+}
+
+// D = A (16x8, row) * B (8x8, col) + D, fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_16x8x8_f16f32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
+{
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, "
+                 "{%0, %1, %2, %3};\n"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// D = A (16x16, row) * B (16x8, col) + D, fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_16x8x16_f16f32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                   uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};\n"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 }  // namespace umma

@@ -86,6 +86,7 @@ constexpr int kLStageW = 24;       // staged left columns [w0-8, w0+16)
 constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 4;       // staging ring depth
+constexpr int kBurst = 4;          // MMA rounds between dependency polls
 
 struct StemParams {
     const __half* vol;    // volume mode: [B, G, D, H, W]
@@ -107,6 +108,7 @@ struct StemParams {
     int tpj;                  // producer tasks per job (each a range of right tiles)
     int raw_w_smem;           // 1: weights are staged through shared memory at set-up
     int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
+    int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
     int n_rbox;               // right boxes of 64 columns per job
     uint32_t tmem_cols;
     uint32_t off_b, off_vol, vol_buf_bytes, lbo_vol, off_stage, stage_slot_bytes, off_bar;
@@ -193,17 +195,36 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* er
     return __all_sync(0xffffffffu, ok);
 }
 
+// 8x8 transpose of 32-bit elements within each group of 8 lanes (lanes
+// 8g .. 8g+7): on return, e[j] of lane 8g + i is what e[i] of lane 8g + j
+// held on entry.  Three butterfly rounds of 4 shuffles.
+__device__ __forceinline__ void transpose8x8(uint32_t (&e)[8], int lane)
+{
+#pragma unroll
+    for (int s = 4; s >= 1; s >>= 1) {
+        const bool upper = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i & s) continue;
+            const uint32_t send = upper ? e[i] : e[i + s];
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, s);
+            if (upper) e[i] = recv;
+            else e[i + s] = recv;
+        }
+    }
+}
+
 // Scale, round and store one 16x8 tile of correlation accumulators (8 groups
 // per slot) into the volume buffer vsa ([d' = d+1][w'][8 groups] rows).
 // Accumulator slot s of thread t is row m + 8 (s >> 1) (volume column
 // w' = m + 8 (s >> 1)), column 2q + (s & 1) of right tile jt (staged right
 // index 8 jt + 2q + (s & 1)), i.e. disparity d = 8 ceil(D/8) - 1 + w' - index.
+template <bool DIV>
 __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float (&acc)[8][4], uint32_t vsa,
                                                 int jt, int lane)
 {
     const int m = lane >> 2, q = lane & 3;
     const int dbase = 8 * (p.n_tiles - 2) - 1;
-    const bool div = p.scale_div != 0;
     const float inv_cg = p.inv_cg, cgf = static_cast<float>(p.Cg);
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
@@ -213,8 +234,8 @@ __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float
             uint32_t h[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float v0 = div ? __fdiv_rn(acc[2 * k][s], cgf) : __fmul_rn(acc[2 * k][s], inv_cg);
-                const float v1 = div ? __fdiv_rn(acc[2 * k + 1][s], cgf) : __fmul_rn(acc[2 * k + 1][s], inv_cg);
+                const float v0 = DIV ? __fdiv_rn(acc[2 * k][s], cgf) : __fmul_rn(acc[2 * k][s], inv_cg);
+                const float v1 = DIV ? __fdiv_rn(acc[2 * k + 1][s], cgf) : __fmul_rn(acc[2 * k + 1][s], inv_cg);
                 const __half2 h2 = __floats2half2_rn(v0, v1);
                 h[k] = *reinterpret_cast<const uint32_t*>(&h2);
             }
@@ -251,9 +272,11 @@ __device__ __forceinline__ uint32_t rchunk(uint32_t rb, int r, int jt, uint32_t 
 // products in its own order, so a volume value can differ from the CorrVolume
 // kernels' sequential fp32 fma chain in the last fp32 bits (and, rarely, by
 // one fp16 ulp after rounding).
-// KM = 8: Cg <= 8 (m16n8k8); KM = 16: 8 < Cg <= 16 (m16n8k16).  Channels
-// >= Cg read zeros (A: predicated loads; B: a zeroed 128-byte row).
-template <int KM>
+// KM = 8: Cg <= 8 (m16n8k8); KM = 16: 8 < Cg <= 16 (m16n8k16).  FULL: Cg ==
+// KM (no absent channels); otherwise channels >= Cg read zeros (A:
+// predicated loads; B: a zeroed 128-byte row).  DIV: scale by / Cg instead
+// of * (1 / Cg) (the CorrVolume kernel the reference would pick).
+template <int KM, bool FULL, bool DIV>
 __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                               uint32_t vsa, int jt0, int jt1, int lane)
 {
@@ -273,8 +296,8 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
         for (int r = 0; r < NA; ++r) {
             const int c0 = 2 * q + 8 * (r >> 1);
             const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * (m + 7 + 8 * (r & 1)));
-            const unsigned short lo = c0 < Cg ? ld_shared_u16(la) : 0;
-            const unsigned short hi = c0 + 1 < Cg ? ld_shared_u16(la + kLRowBytes) : 0;
+            const unsigned short lo = (FULL || c0 < Cg) ? ld_shared_u16(la) : 0;
+            const unsigned short hi = (FULL || c0 + 1 < Cg) ? ld_shared_u16(la + kLRowBytes) : 0;
             a[e][r] = pack_b16x2(lo, hi);
         }
     }
@@ -288,39 +311,54 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
     for (int k = 0; k < NI; ++k) {
         const int e = KM == 8 ? 4 * k + mi : 2 * k + (mi >> 1);
         const int c = KM == 8 ? rr : 8 * (mi & 1) + rr;
-        rrow[k] = c < Cg ? e * Cg + c : -1;
+        rrow[k] = (FULL || c < Cg) ? e * Cg + c : -1;
         rb[k] = rrow[k] >= 0 ? slot + static_cast<uint32_t>(rrow[k]) * 128u : zero_row;
     }
 
-    for (int jt = jt0; jt < jt1; ++jt) {
+    // KM = 8: two tiles at a time, both tiles' fragments and MMAs in flight
+    // before either is scaled and stored (KM = 16 holds twice the fragments
+    // and takes one tile at a time to stay within the register budget).
+    constexpr int TT = KM == 8 ? 2 : 1;
+    for (int jt = jt0; jt < jt1; jt += TT) {
+        const int nt = jt + 1 < jt1 ? TT : 1;
         __syncwarp();
-        uint32_t b[8][NB];
+        uint32_t b[TT][8][NB];
 #pragma unroll
-        for (int k = 0; k < NI; ++k) {
-            uint32_t r4[4];
-            const uint32_t addr = rrow[k] >= 0 ? rchunk(rb[k], rrow[k], jt, p.rbox_bytes)
-                                               : rb[k] + (static_cast<uint32_t>(jt & 7) << 4);
-            ldmatrix_x4_trans(addr, r4);
+        for (int u = 0; u < TT; ++u) {
+            if (u >= nt) break;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (KM == 8) b[4 * k + i][0] = r4[i];
-                else b[2 * k + (i >> 1)][i & 1] = r4[i];
+            for (int k = 0; k < NI; ++k) {
+                uint32_t r4[4];
+                const uint32_t addr = (FULL || rrow[k] >= 0) ? rchunk(rb[k], rrow[k], jt + u, p.rbox_bytes)
+                                                             : rb[k] + (static_cast<uint32_t>((jt + u) & 7) << 4);
+                ldmatrix_x4_trans(addr, r4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (KM == 8) b[u][4 * k + i][0] = r4[i];
+                    else b[u][2 * k + (i >> 1)][i & 1] = r4[i];
+                }
             }
         }
-        float acc[8][4];
+        float acc[TT][8][4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int u = 0; u < TT; ++u) {
+            if (u >= nt) break;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) acc[e][s] = 0.0f;
-            if (KM == 8) mma_16x8x8_f16f32(acc[e], a[e][0], a[e][1], b[e][0]);
-            else mma_16x8x16_f16f32(acc[e], a[e][0], a[e][1], a[e][2], a[e][3], b[e][0], b[e][NB - 1]);
+            for (int e = 0; e < 8; ++e) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) acc[u][e][s] = 0.0f;
+                if (KM == 8) mma_16x8x8_f16f32(acc[u][e], a[e][0], a[e][1], b[u][e][0]);
+                else mma_16x8x16_f16f32(acc[u][e], a[e][0], a[e][1], a[e][2], a[e][3], b[u][e][0], b[u][e][NB - 1]);
+            }
         }
-        store_corr_tile(p, acc, vsa, jt, lane);
+        store_corr_tile<DIV>(p, acc[0], vsa, jt, lane);
+        if (TT == 2 && nt == 2) store_corr_tile<DIV>(p, acc[TT - 1], vsa, jt + 1, lane);
     }
 }
 
 // Cg > 16: the channels run through the tensor core in chunks of 16 (the
 // last one zero-padded), with the fragments of each chunk loaded per tile.
+template <bool DIV>
 __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                                    uint32_t vsa, int jt0, int jt1, int lane)
 {
@@ -364,11 +402,31 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                 mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
             }
         }
-        store_corr_tile(p, acc, vsa, jt, lane);
+        store_corr_tile<DIV>(p, acc, vsa, jt, lane);
     }
 }
 
-template <int COUTP, bool FUSED>
+// Correlation variants (a kernel template parameter, so each instantiation
+// carries only its own producer path): 1: Cg == 8, 2: Cg < 8, 3: Cg == 16,
+// 4: 8 < Cg < 16, 5: Cg > 16.
+template <int CORR, bool DIV>
+__device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, uint32_t zero_row, uint32_t vsa,
+                                          int jt0, int jt1, int lane)
+{
+    if constexpr (CORR == 1) corr_task_mma<8, true, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 2) corr_task_mma<8, false, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 3) corr_task_mma<16, true, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 4) corr_task_mma<16, false, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else corr_task_mma_wide<DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+}
+
+inline int corr_variant(int Cg)
+{
+    return Cg == 8 ? 1 : Cg < 8 ? 2 : Cg == 16 ? 3 : Cg < 16 ? 4 : 5;
+}
+
+// CORR: correlation variant (fused mode; 0 in volume mode), DIV: scale mode.
+template <int COUTP, bool FUSED, int CORR, bool DIV>
 __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_constant__ StemParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -526,106 +584,86 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_addr(&acc_empty[m]));
                 const int d = m * 16 + dsub;
-                if (r >= r0 && r < r1 && d < p.D && w < p.W) {
-                    __half* op = p.out + ((i64(b) * p.Cout) * p.D + d) * plane_out + i64(r - p.out_row0) * p.W + w;
+                if (r < r0 || r >= r1) continue;  // warp-uniform
+                // fp16 results, packed as (o, o + 1) pairs
+                uint32_t ph[COUTP / 2];
 #pragma unroll
-                    for (int o = 0; o < COUTP; ++o)
-                        if (o < p.Cout)
-                            op[o * ostride] = __float2half_rn(act_apply(__uint_as_float(acc[o]) + bias[o], p.act));
+                for (int k = 0; k < COUTP / 2; ++k) {
+                    const __half2 h2 =
+                        __floats2half2_rn(act_apply(__uint_as_float(acc[2 * k]) + bias[2 * k], p.act),
+                                          act_apply(__uint_as_float(acc[2 * k + 1]) + bias[2 * k + 1], p.act));
+                    ph[k] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                __half* orow = p.out + ((i64(b) * p.Cout) * p.D + d) * plane_out + i64(r - p.out_row0) * p.W;
+                if (p.out_vec) {
+                    // The 8 lanes of a lane group hold the 8 columns of one
+                    // disparity: transpose blocks of 8 o-pairs among them so
+                    // each lane ends with 8 columns of two channels, written
+                    // as two 16-byte rows.
+#pragma unroll
+                    for (int blk = 0; blk < COUTP / 16; ++blk) {
+                        uint32_t e[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) e[i] = ph[8 * blk + i];
+                        transpose8x8(e, lane);
+                        const int o0 = 16 * blk + 2 * (lane & 7);
+                        const uint4 lo = make_uint4(__byte_perm(e[0], e[1], 0x5410), __byte_perm(e[2], e[3], 0x5410),
+                                                    __byte_perm(e[4], e[5], 0x5410), __byte_perm(e[6], e[7], 0x5410));
+                        const uint4 hi = make_uint4(__byte_perm(e[0], e[1], 0x7632), __byte_perm(e[2], e[3], 0x7632),
+                                                    __byte_perm(e[4], e[5], 0x7632), __byte_perm(e[6], e[7], 0x7632));
+                        if (d < p.D && o0 < p.Cout) *reinterpret_cast<uint4*>(orow + o0 * ostride + w0) = lo;
+                        if (d < p.D && o0 + 1 < p.Cout) *reinterpret_cast<uint4*>(orow + (o0 + 1) * ostride + w0) = hi;
+                    }
+                } else if (d < p.D && w < p.W) {
+#pragma unroll
+                    for (int k = 0; k < COUTP / 2; ++k) {
+                        const __half2 h2 = *reinterpret_cast<const __half2*>(&ph[k]);
+                        if (2 * k < p.Cout) orow[(2 * k) * ostride + w] = __low2half(h2);
+                        if (2 * k + 1 < p.Cout) orow[(2 * k + 1) * ostride + w] = __high2half(h2);
+                    }
                 }
             }
         }
     } else if (warp == kMmaWarp) {
         // ======================= MMA issue =======================
-        // A "chain" is one (volume row, M-block): nsteps MMAs accumulating into
-        // the same tensor-memory columns.  Back to back, such a chain runs at
-        // ~93 cycles per MMA instead of the ~56 an independent MMA costs, so
-        // chains are issued staggered: the second half of chain k-1
-        // interleaved with the first half of chain k.  Chain k needs only what
-        // chain k-1's predecessors released (its volume row; the drain of its
-        // slot two rows back), so there is no bubble at M-block or row
-        // boundaries.  The whole warp runs the (uniform) schedule; one elected
-        // lane issues.
-        constexpr uint32_t idesc = idesc_f16_f32(128, N);
-        const int S = p.nsteps;
-        const int S1 = (S + 1) / 2;
-        const int n_chains = n_iter * p.n_mb;
-        const bool stagger = p.n_mb > 1;  // one M-block: chain k waits on chain k-1's drain
-        const uint64_t vol_base = smem_addr(sVol) >> 4;
-        const uint64_t b_base = smem_addr(sB) >> 4;
-        bool ok = true;
-        bool prev_live = false, prev_active = false;
-        int prev_m = 0, prev_it = 0;
-        uint64_t prev_a = 0, prev_b = 0;
-        uint32_t prev_d = 0;
-        auto issue_range = [&](bool active, uint64_t a_add, uint64_t b_add, uint32_t d, int s0, int s1) {
-            if (!active) return;
-            for (int st = s0; st < s1; ++st) {
-                const uint64_t ad = p.tmplA[st] + a_add, bd = p.tmplB[st] + b_add;
-                if (elect_one()) mma_f16_ss(d, ad, bd, idesc, 1);
-                __syncwarp();
-            }
-        };
-        auto retire_prev = [&]() {  // second half issued: signal its consumers
-            if (elect_one()) {
-                mma_commit(smem_addr(&acc_full[prev_m]));
-                if (prev_m == p.n_mb - 1) mma_commit(smem_addr(&vol_empty[prev_it & 1]));
-            }
-            __syncwarp();
-            prev_live = false;
-        };
-        for (int k = 0; k < n_chains && ok; ++k) {
-            const int it = k / p.n_mb, m = k - it * p.n_mb;
-            const int u = u_first + it;
-            if (m == 0) {
-                const uint32_t bar = smem_addr(&vol_full[it & 1]);
-                if (prev_live && !__all_sync(0xffffffffu, mbar_try_wait(bar, (it >> 1) & 1))) {
-                    // the next row is not produced yet: finish the previous chain alone
-                    issue_range(prev_active, prev_a, prev_b, prev_d, S1, S);
-                    retire_prev();
-                }
-                if (!warp_wait(bar, (it >> 1) & 1, p.err, 2)) { ok = false; break; }
-            }
-            if (!stagger && prev_live) {
-                issue_range(prev_active, prev_a, prev_b, prev_d, S1, S);
-                retire_prev();
-            }
-            if (it > 0 && !warp_wait(smem_addr(&acc_empty[m]), (it - 1) & 1, p.err, 3)) { ok = false; break; }
-            fence_after_sync();
-            const bool active = (u >= 0 && u < p.H);
-            const int rot = (((1 - u) % 3) + 3) % 3;
-            const uint64_t b_add = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
-            const uint64_t a_add = vol_base + static_cast<uint64_t>(((it & 1) * p.vol_buf_bytes + m * 16 * kWtp * 16) >> 4);
-            const uint32_t d = tmem_base + m * N;
-            if (prev_live) {
-                // interleave: previous chain steps [S1, S) with this chain's [0, S1)
-                for (int j = 0; j < S1; ++j) {
-                    const bool do_prev = prev_active && S1 + j < S;
-                    const uint64_t pa = p.tmplA[S1 + j < S ? S1 + j : 0] + prev_a;
-                    const uint64_t pb = p.tmplB[S1 + j < S ? S1 + j : 0] + prev_b;
-                    const uint64_t ca = p.tmplA[j] + a_add, cb = p.tmplB[j] + b_add;
-                    if (elect_one()) {
-                        if (do_prev) mma_f16_ss(prev_d, pa, pb, idesc, 1);
-                        if (active) mma_f16_ss(d, ca, cb, idesc, 1);
+        // Row by row: once volume row it is produced (vol_full) and the
+        // epilogue has drained every M-block's slot of row it-1 (acc_empty),
+        // issue the row's nsteps K-steps with the n_mb M-blocks interleaved
+        // inside each step.  MMAs into the same accumulator back to back are
+        // latency-bound (~150 cycles each); independent ones run at the
+        // shared-memory bound (~56 cycles for M=128, N=96), which this order
+        // reaches from n_mb = 3 on.  Lane 0 alone runs the loop: a warp-wide
+        // elect + __syncwarp around every MMA, or a scheduler loop with
+        // per-MMA bookkeeping, halve to quarter the issue rate (measured).
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(128, N);
+            const int S = p.nsteps;
+            const uint64_t vol_base = smem_addr(sVol) >> 4;
+            const uint64_t b_base = smem_addr(sB) >> 4;
+            constexpr uint64_t mb_step = (16 * kWtp * 16) >> 4;  // one M-block along D
+            for (int it = 0; it < n_iter; ++it) {
+                if (!wait_or_fail(smem_addr(&vol_full[it & 1]), (it >> 1) & 1, p.err, 2)) break;
+                bool ok = true;
+                for (int m = 0; m < p.n_mb && it > 0 && ok; ++m)
+                    ok = wait_or_fail(smem_addr(&acc_empty[m]), (it - 1) & 1, p.err, 3);
+                if (!ok) break;
+                fence_after_sync();
+                const int u = u_first + it;
+                if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
+                    const int rot = (((1 - u) % 3) + 3) % 3;
+                    const uint64_t a0 = vol_base + static_cast<uint64_t>(((it & 1) * p.vol_buf_bytes) >> 4);
+                    const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
+                    for (int st = 0; st < S; ++st) {
+                        const uint64_t a = p.tmplA[st] + a0, bd = p.tmplB[st] + b0;
+                        for (int m = 0; m < p.n_mb; ++m)
+                            mma_f16_ss(tmem_base + m * N, a + m * mb_step, bd, idesc, 1);
                     }
-                    __syncwarp();
                 }
-                retire_prev();
-            } else {
-                issue_range(active, a_add, b_add, d, 0, S1);
+                for (int m = 0; m < p.n_mb; ++m) mma_commit(smem_addr(&acc_full[m]));
+                mma_commit(smem_addr(&vol_empty[it & 1]));
             }
-            prev_live = true;
-            prev_active = active;
-            prev_m = m;
-            prev_it = it;
-            prev_a = a_add;
-            prev_b = b_add;
-            prev_d = d;
         }
-        if (ok && prev_live) {
-            issue_range(prev_active, prev_a, prev_b, prev_d, S1, S);
-            retire_prev();
-        }
+        __syncwarp();
     } else if (warp == kLoadWarp) {
         // ======================= loader =======================
         // Job j = (volume row uv0 + j / KG, group octet j % KG) -> slot j % NS,
@@ -737,9 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         for (int h = ((pw - job * p.tpj) % kProdWarps + kProdWarps) % kProdWarps; h < p.tpj;
                              h += kProdWarps) {
                             const int jt0 = (h * p.n_tiles) / p.tpj, jt1 = ((h + 1) * p.n_tiles) / p.tpj;
-                            if (p.Cg <= 8) corr_task_mma<8>(p, sbase, zero_row, vsa, jt0, jt1, lane);
-                            else if (p.Cg <= 16) corr_task_mma<16>(p, sbase, zero_row, vsa, jt0, jt1, lane);
-                            else corr_task_mma_wide(p, sbase, zero_row, vsa, jt0, jt1, lane);
+                            corr_task<CORR, DIV>(p, sbase, zero_row, vsa, jt0, jt1, lane);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
@@ -882,9 +918,11 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     off += fused ? p.n_slots * p.stage_slot_bytes : 0;
     const size_t smem = off;
     if (smem > static_cast<size_t>(dev.smem_optin)) return WW_ERR_UNSUPPORTED;
-    // Tasks per job: enough to give every producer warp work in each volume
-    // row, at most one per right tile.
-    p.tpj = std::min(p.n_tiles, std::max(1, (kProdWarps + KG - 1) / KG));
+    // Tasks per job.  A job's staging slot is refilled only when all its
+    // tasks are done, so spreading a job over many warps (short job latency)
+    // keeps the staging ring moving.
+    p.tpj = p.n_tiles;  // one right tile per task: a job is spread over all producer warps
+    p.out_vec = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     {
         const size_t wbytes = static_cast<size_t>(Cout) * G * 54;
         p.raw_w_smem = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0) &&
@@ -930,8 +968,16 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
         kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
         return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
     };
-    if (coutp == 16) return fused ? launch(stem_tc_kernel<16, true>) : launch(stem_tc_kernel<16, false>);
-    return fused ? launch(stem_tc_kernel<32, true>) : launch(stem_tc_kernel<32, false>);
+    if (!fused) return coutp == 16 ? launch(stem_tc_kernel<16, false, 0, false>) : launch(stem_tc_kernel<32, false, 0, false>);
+    const int cv = corr_variant(Cg);
+    const bool dv = p.scale_div != 0;
+#define WW_FUSED_CASE(CP, CV)                                                                              \
+    if (coutp == CP && cv == CV)                                                                           \
+        return dv ? launch(stem_tc_kernel<CP, true, CV, true>) : launch(stem_tc_kernel<CP, true, CV, false>);
+    WW_FUSED_CASE(16, 1) WW_FUSED_CASE(16, 2) WW_FUSED_CASE(16, 3) WW_FUSED_CASE(16, 4) WW_FUSED_CASE(16, 5)
+    WW_FUSED_CASE(32, 1) WW_FUSED_CASE(32, 2) WW_FUSED_CASE(32, 3) WW_FUSED_CASE(32, 4) WW_FUSED_CASE(32, 5)
+#undef WW_FUSED_CASE
+    return WW_ERR_UNSUPPORTED;
 }
 
 }  // namespace ww

@@ -220,6 +220,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t saddr, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking poll: has the phase with the given parity completed?
+// (try_wait may suspend the thread for a system-defined time when it has
+// not; a polling loop that interleaves other work must use test_wait.)
+__device__ __forceinline__ bool mbar_test_wait(uint32_t saddr, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(saddr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // try_wait that lets the hardware suspend the thread for up to `hint_ns`
 // nanoseconds (it resumes as soon as the phase completes), so waiting warps
 // do not spin through issue slots the working warps need.

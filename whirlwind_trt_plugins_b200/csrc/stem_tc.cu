@@ -31,8 +31,9 @@
 //                       row u's contribution to output rows u+1, u, u-1.  The
 //                       (kd, kw) taps are start-address shifts of the same buffer.
 //   epilogue (4 warps)  when output row u-1 is complete, read its accumulators
-//                       out of tensor memory, add the bias, apply the
-//                       activation, store fp16, and zero the slot for reuse.
+//                       out of tensor memory (releasing the slot at once: the
+//                       MMA warp restarts it with accumulate = 0), add the
+//                       bias, apply the activation and store fp16.
 //
 // Tensor-memory accumulators: per M-block three Cout-column slots; output row
 // r lives in slot r mod 3.  The MMA always writes all three slots, so which kh
@@ -54,7 +55,7 @@
 //   vol_full[2]     producers -> MMA        volume buffer ready
 //   vol_empty[2]    MMA (commit) -> producers   all MMAs reading it finished
 //   acc_full[m]     MMA (commit) -> epilogue    row u-1 of M-block m complete
-//   acc_empty[m]    epilogue -> MMA             row u-1's slot drained and zeroed
+//   acc_empty[m]    epilogue -> MMA             row u-1's slot read out
 // A wait that expires records an error code in the device error word; the
 // waiting role stops, the others run into their own bounded waits, and the
 // CTA winds down and frees its tensor memory.
@@ -67,7 +68,6 @@
 
 namespace ww {
 
-int corr_scale_div_grouped(bool is_half, int B, int C, int G, int H, int W, int D, int sm_count) noexcept;
 
 namespace {
 
@@ -85,8 +85,8 @@ constexpr int kMaxMB = 10;         // M-blocks per CTA (TMEM: kMaxMB * 3 * 16 <=
 constexpr int kLStageW = 24;       // staged left columns [w0-8, w0+16)
 constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
-constexpr int kMaxSlots = 4;       // staging ring depth
-constexpr int kBurst = 4;          // MMA rounds between dependency polls
+constexpr int kMaxSlots = 8;       // staging ring depth
+constexpr int kDrain = 3;          // M-blocks the epilogue drains before storing them
 
 struct StemParams {
     const __half* vol;    // volume mode: [B, G, D, H, W]
@@ -99,7 +99,6 @@ struct StemParams {
     int B, C, G, H, W, D, Cout, act;
     int in_row0, in_rows, out_row0, out_rows;
     int Cg, KG, Dp, n_mb, nsteps, strip, n_strips, n_wtiles;
-    int scale_div;
     float inv_cg;
     int vec_ok;
     int rstage_w;             // staged right columns
@@ -116,10 +115,16 @@ struct StemParams {
     uint32_t off_l;           // left rows within a slot
     uint32_t stage_tx;        // bytes a job's TMA copies deliver
     uint32_t off_zero;        // 128 zero bytes (rows of absent channels)
+    uint32_t off_bias;        // COUTP fp32 biases (zero past Cout)
     // Per K-step descriptor templates with a zero base address: A relative to a
     // volume buffer, B relative to the B image.  Read with uniform loads.
     uint64_t tmplA[kMaxSteps];
     uint64_t tmplB[kMaxSteps];
+    // Per (step, chunk): weight offset of the chunk's tap and octet within an
+    // output channel's [G][27] row (-1: zero-weight partner), and the number
+    // of real groups in the octet.
+    int step_off[2 * kMaxSteps];
+    int step_gv[2 * kMaxSteps];
     // TMA maps of the left / right features (4-D: x = W, y = row, z = channel,
     // w = batch); boxes [24] x [8 Cg] (left) and [64] x [8 Cg] (right, swizzled).
     CUtensorMap tmap_l;
@@ -219,13 +224,12 @@ __device__ __forceinline__ void transpose8x8(uint32_t (&e)[8], int lane)
 // Accumulator slot s of thread t is row m + 8 (s >> 1) (volume column
 // w' = m + 8 (s >> 1)), column 2q + (s & 1) of right tile jt (staged right
 // index 8 jt + 2q + (s & 1)), i.e. disparity d = 8 ceil(D/8) - 1 + w' - index.
-template <bool DIV>
 __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float (&acc)[8][4], uint32_t vsa,
                                                 int jt, int lane)
 {
     const int m = lane >> 2, q = lane & 3;
     const int dbase = 8 * (p.n_tiles - 2) - 1;
-    const float inv_cg = p.inv_cg, cgf = static_cast<float>(p.Cg);
+    const float inv_cg = p.inv_cg;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int wp = m + 8 * (s >> 1);
@@ -234,8 +238,8 @@ __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float
             uint32_t h[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float v0 = DIV ? __fdiv_rn(acc[2 * k][s], cgf) : __fmul_rn(acc[2 * k][s], inv_cg);
-                const float v1 = DIV ? __fdiv_rn(acc[2 * k + 1][s], cgf) : __fmul_rn(acc[2 * k + 1][s], inv_cg);
+                const float v0 = __fmul_rn(acc[2 * k][s], inv_cg);
+                const float v1 = __fmul_rn(acc[2 * k + 1][s], inv_cg);
                 const __half2 h2 = __floats2half2_rn(v0, v1);
                 h[k] = *reinterpret_cast<const uint32_t*>(&h2);
             }
@@ -274,9 +278,8 @@ __device__ __forceinline__ uint32_t rchunk(uint32_t rb, int r, int jt, uint32_t 
 // one fp16 ulp after rounding).
 // KM = 8: Cg <= 8 (m16n8k8); KM = 16: 8 < Cg <= 16 (m16n8k16).  FULL: Cg ==
 // KM (no absent channels); otherwise channels >= Cg read zeros (A:
-// predicated loads; B: a zeroed 128-byte row).  DIV: scale by / Cg instead
-// of * (1 / Cg) (the CorrVolume kernel the reference would pick).
-template <int KM, bool FULL, bool DIV>
+// predicated loads; B: a zeroed 128-byte row).
+template <int KM, bool FULL>
 __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                               uint32_t vsa, int jt0, int jt1, int lane)
 {
@@ -315,50 +318,35 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
         rb[k] = rrow[k] >= 0 ? slot + static_cast<uint32_t>(rrow[k]) * 128u : zero_row;
     }
 
-    // KM = 8: two tiles at a time, both tiles' fragments and MMAs in flight
-    // before either is scaled and stored (KM = 16 holds twice the fragments
-    // and takes one tile at a time to stay within the register budget).
-    constexpr int TT = KM == 8 ? 2 : 1;
-    for (int jt = jt0; jt < jt1; jt += TT) {
-        const int nt = jt + 1 < jt1 ? TT : 1;
+    for (int jt = jt0; jt < jt1; ++jt) {
         __syncwarp();
-        uint32_t b[TT][8][NB];
+        uint32_t b[8][NB];
 #pragma unroll
-        for (int u = 0; u < TT; ++u) {
-            if (u >= nt) break;
+        for (int k = 0; k < NI; ++k) {
+            uint32_t r4[4];
+            const uint32_t addr = (FULL || rrow[k] >= 0) ? rchunk(rb[k], rrow[k], jt, p.rbox_bytes)
+                                                         : rb[k] + (static_cast<uint32_t>(jt & 7) << 4);
+            ldmatrix_x4_trans(addr, r4);
 #pragma unroll
-            for (int k = 0; k < NI; ++k) {
-                uint32_t r4[4];
-                const uint32_t addr = (FULL || rrow[k] >= 0) ? rchunk(rb[k], rrow[k], jt + u, p.rbox_bytes)
-                                                             : rb[k] + (static_cast<uint32_t>((jt + u) & 7) << 4);
-                ldmatrix_x4_trans(addr, r4);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (KM == 8) b[u][4 * k + i][0] = r4[i];
-                    else b[u][2 * k + (i >> 1)][i & 1] = r4[i];
-                }
+            for (int i = 0; i < 4; ++i) {
+                if (KM == 8) b[4 * k + i][0] = r4[i];
+                else b[2 * k + (i >> 1)][i & 1] = r4[i];
             }
         }
-        float acc[TT][8][4];
+        float acc[8][4];
 #pragma unroll
-        for (int u = 0; u < TT; ++u) {
-            if (u >= nt) break;
+        for (int e = 0; e < 8; ++e) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-#pragma unroll
-                for (int s = 0; s < 4; ++s) acc[u][e][s] = 0.0f;
-                if (KM == 8) mma_16x8x8_f16f32(acc[u][e], a[e][0], a[e][1], b[u][e][0]);
-                else mma_16x8x16_f16f32(acc[u][e], a[e][0], a[e][1], a[e][2], a[e][3], b[u][e][0], b[u][e][NB - 1]);
-            }
+            for (int s = 0; s < 4; ++s) acc[e][s] = 0.0f;
+            if (KM == 8) mma_16x8x8_f16f32(acc[e], a[e][0], a[e][1], b[e][0]);
+            else mma_16x8x16_f16f32(acc[e], a[e][0], a[e][1], a[e][2], a[e][3], b[e][0], b[e][NB - 1]);
         }
-        store_corr_tile<DIV>(p, acc[0], vsa, jt, lane);
-        if (TT == 2 && nt == 2) store_corr_tile<DIV>(p, acc[TT - 1], vsa, jt + 1, lane);
+        store_corr_tile(p, acc, vsa, jt, lane);
     }
 }
 
 // Cg > 16: the channels run through the tensor core in chunks of 16 (the
 // last one zero-padded), with the fragments of each chunk loaded per tile.
-template <bool DIV>
 __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                                    uint32_t vsa, int jt0, int jt1, int lane)
 {
@@ -402,22 +390,22 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                 mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
             }
         }
-        store_corr_tile<DIV>(p, acc, vsa, jt, lane);
+        store_corr_tile(p, acc, vsa, jt, lane);
     }
 }
 
 // Correlation variants (a kernel template parameter, so each instantiation
 // carries only its own producer path): 1: Cg == 8, 2: Cg < 8, 3: Cg == 16,
 // 4: 8 < Cg < 16, 5: Cg > 16.
-template <int CORR, bool DIV>
+template <int CORR>
 __device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, uint32_t zero_row, uint32_t vsa,
                                           int jt0, int jt1, int lane)
 {
-    if constexpr (CORR == 1) corr_task_mma<8, true, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 2) corr_task_mma<8, false, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 3) corr_task_mma<16, true, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 4) corr_task_mma<16, false, DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else corr_task_mma_wide<DIV>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    if constexpr (CORR == 1) corr_task_mma<8, true>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 2) corr_task_mma<8, false>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 3) corr_task_mma<16, true>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else if constexpr (CORR == 4) corr_task_mma<16, false>(p, slot, zero_row, vsa, jt0, jt1, lane);
+    else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane);
 }
 
 inline int corr_variant(int Cg)
@@ -425,8 +413,8 @@ inline int corr_variant(int Cg)
     return Cg == 8 ? 1 : Cg < 8 ? 2 : Cg == 16 ? 3 : Cg < 16 ? 4 : 5;
 }
 
-// CORR: correlation variant (fused mode; 0 in volume mode), DIV: scale mode.
-template <int COUTP, bool FUSED, int CORR, bool DIV>
+// CORR: correlation variant (fused mode; 0 in volume mode).
+template <int COUTP, bool FUSED, int CORR>
 __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_constant__ StemParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -487,8 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     // shared memory (the volume and staging regions, unused until set-up
     // ends) with coalesced 16-byte copies; the B image is then gathered from
     // there instead of with scattered 2-byte global loads.
-    const __half* wsrc = p.w;
-    if (p.raw_w_smem) {
+    const bool wsm = p.raw_w_smem != 0;
+    if (wsm) {
         const uint32_t wbytes = static_cast<uint32_t>(p.Cout * p.G * 54);
         const uint32_t dst0 = smem_addr(sVol);
         for (uint32_t i = threadIdx.x * 16; i < wbytes; i += kThreads * 16)
@@ -498,30 +486,35 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                          : "memory");
         asm volatile("cp.async.wait_all;\n" ::: "memory");
         __syncthreads();
-        wsrc = reinterpret_cast<const __half*>(sVol);
     }
-    // B image: step s, chunk c, row n (= blk*COUTP + o), 8 fp16 of consecutive groups.
-    for (int i = threadIdx.x; i < p.nsteps * 2 * NR; i += kThreads) {
-        const int n = i % NR;
-        const int sc = i / NR;
-        const int c = sc & 1, s = sc >> 1;
-        const StepInfo si = step_info(s, p.KG);
-        const int tap = c ? si.t1 : si.t0;
-        const int kg = c ? si.kg1 : si.kg0;
-        const int blk = n / COUTP, o = n - blk * COUTP;
-        const int kh = (2 - blk + 3) % 3;
-        __align__(16) __half v[8];
+    // B image: entry (step s, chunk c, row n = blk * COUTP + o) holds the 8
+    // fp16 weights of the chunk's group octet for output channel o and tap
+    // (kd, kh, kw); blocks blk = 0..4 are [kh2, kh1, kh0, kh2, kh1].  The
+    // host precomputes each chunk's tap offset (step_off; -1 for a
+    // zero-weight partner) and valid group count (step_gv).
+    {
+        const uint32_t raw = smem_addr(sVol);
+        const unsigned short* wg = reinterpret_cast<const unsigned short*>(p.w);
+        const int g27 = p.G * 27;
+        for (int i = threadIdx.x; i < p.nsteps * 2 * NR; i += kThreads) {
+            const int n = i % NR, sc = i / NR;
+            const int blk = n / COUTP, o = n - blk * COUTP;
+            const int kh = (blk == 2) ? 0 : ((blk == 1 || blk == 4) ? 1 : 2);
+            const int toff = p.step_off[sc], gv = p.step_gv[sc];
+            uint32_t v[4] = {0u, 0u, 0u, 0u};
+            if (toff >= 0 && o < p.Cout) {
+                const int base = o * g27 + kh * 3 + toff;
+                unsigned short h[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int g = kg * 8 + e;
-            __half x = __float2half_rn(0.0f);
-            if (tap >= 0 && o < p.Cout && g < p.G) {
-                const int kd = tap / 3, kw = tap - 3 * (tap / 3);
-                x = wsrc[(i64(o) * p.G + g) * 27 + kd * 9 + kh * 3 + kw];
+                for (int e = 0; e < 8; ++e)
+                    h[e] = e < gv ? (wsm ? ld_shared_u16(raw + 2u * static_cast<uint32_t>(base + e * 27))
+                                         : wg[base + e * 27])
+                                  : static_cast<unsigned short>(0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[q] = pack_b16x2(h[2 * q], h[2 * q + 1]);
             }
-            v[e] = x;
+            st_shared_v4(smem_addr(sB) + 16u * static_cast<uint32_t>(i), v[0], v[1], v[2], v[3]);
         }
-        *reinterpret_cast<uint4*>(sB + static_cast<size_t>(i) * 16) = *reinterpret_cast<uint4*>(v);
     }
     __syncthreads();  // the staged weights are consumed before the region is zeroed
     // Both volume buffers start as zeros: halo planes and padding stay zero;
@@ -530,6 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         *reinterpret_cast<uint4*>(sVol + i) = make_uint4(0, 0, 0, 0);
     for (uint32_t i = threadIdx.x * 16; i < 128u; i += kThreads * 16)
         *reinterpret_cast<uint4*>(smem + p.off_zero + i) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < COUTP)
+        reinterpret_cast<float*>(smem + p.off_bias)[threadIdx.x] =
+            threadIdx.x < p.Cout ? __half2float(p.bias[threadIdx.x]) : 0.0f;
 
     fence_proxy_async_smem();
     fence_before_sync();
@@ -550,76 +546,89 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
 
     if (warp < kEpiWarps) {
         // ======================= epilogue =======================
+        // Per volume row: first drain the completed output row of up to
+        // kDrain M-blocks (tensor-memory load, bias + activation, fp16 pack,
+        // zero the slot, release it with acc_empty), so the MMA warp can
+        // start the next row at once; then store them.
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
         const int rr = warp * 32 + lane;  // M row
         const int w = w0 + (rr & 7);
         const int dsub = rr >> 3;         // 0..15
-        float bias[COUTP];
-#pragma unroll
-        for (int o = 0; o < COUTP; ++o) bias[o] = (o < p.Cout) ? __half2float(p.bias[o]) : 0.0f;
+        const float* sbias = reinterpret_cast<const float*>(smem + p.off_bias);
         const int64_t plane_out = i64(p.out_rows) * p.W;
         const int64_t ostride = i64(p.D) * plane_out;
         bool ok = true;
         for (int it = 0; it < n_iter && ok; ++it) {
             const int r = u_first + it - 1;  // output row completed by this volume row
             const int slot = ((r % 3) + 3) % 3;
-            for (int m = 0; m < p.n_mb; ++m) {
-                if (!warp_wait(smem_addr(&acc_full[m]), it & 1, p.err, 1)) { ok = false; break; }
-                fence_after_sync();
-                uint32_t acc[COUTP];
-                const uint32_t col = lane_base + m * N + slot * COUTP;
+            for (int m0 = 0; m0 < p.n_mb && ok; m0 += kDrain) {
+                const int mcnt = min(kDrain, p.n_mb - m0);
+                uint32_t ph[kDrain][COUTP / 2];  // fp16 results, packed as (o, o + 1) pairs
 #pragma unroll
-                for (int c = 0; c < COUTP; c += 16) {
-                    uint32_t v16[16];
-                    tmem_ld16(col + c, v16);
-                    tmem_wait_ld();
+                for (int j = 0; j < kDrain; ++j) {
+                    if (j >= mcnt) break;
+                    const int m = m0 + j;
+                    if (!warp_wait(smem_addr(&acc_full[m]), it & 1, p.err, 1)) { ok = false; break; }
+                    fence_after_sync();
+                    uint32_t acc[COUTP];
+                    const uint32_t col = lane_base + m * N + slot * COUTP;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[c + j] = v16[j];
-                }
-                const uint32_t zeros[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    for (int c = 0; c < COUTP; c += 16) {
+                        uint32_t v16[16];
+                        tmem_ld16(col + c, v16);
 #pragma unroll
-                for (int c = 0; c < COUTP; c += 8) tmem_st8(col + c, zeros);
-                tmem_wait_st();
-                fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_addr(&acc_empty[m]));
-                const int d = m * 16 + dsub;
-                if (r < r0 || r >= r1) continue;  // warp-uniform
-                // fp16 results, packed as (o, o + 1) pairs
-                uint32_t ph[COUTP / 2];
-#pragma unroll
-                for (int k = 0; k < COUTP / 2; ++k) {
-                    const __half2 h2 =
-                        __floats2half2_rn(act_apply(__uint_as_float(acc[2 * k]) + bias[2 * k], p.act),
-                                          act_apply(__uint_as_float(acc[2 * k + 1]) + bias[2 * k + 1], p.act));
-                    ph[k] = *reinterpret_cast<const uint32_t*>(&h2);
-                }
-                __half* orow = p.out + ((i64(b) * p.Cout) * p.D + d) * plane_out + i64(r - p.out_row0) * p.W;
-                if (p.out_vec) {
-                    // The 8 lanes of a lane group hold the 8 columns of one
-                    // disparity: transpose blocks of 8 o-pairs among them so
-                    // each lane ends with 8 columns of two channels, written
-                    // as two 16-byte rows.
-#pragma unroll
-                    for (int blk = 0; blk < COUTP / 16; ++blk) {
-                        uint32_t e[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) e[i] = ph[8 * blk + i];
-                        transpose8x8(e, lane);
-                        const int o0 = 16 * blk + 2 * (lane & 7);
-                        const uint4 lo = make_uint4(__byte_perm(e[0], e[1], 0x5410), __byte_perm(e[2], e[3], 0x5410),
-                                                    __byte_perm(e[4], e[5], 0x5410), __byte_perm(e[6], e[7], 0x5410));
-                        const uint4 hi = make_uint4(__byte_perm(e[0], e[1], 0x7632), __byte_perm(e[2], e[3], 0x7632),
-                                                    __byte_perm(e[4], e[5], 0x7632), __byte_perm(e[6], e[7], 0x7632));
-                        if (d < p.D && o0 < p.Cout) *reinterpret_cast<uint4*>(orow + o0 * ostride + w0) = lo;
-                        if (d < p.D && o0 + 1 < p.Cout) *reinterpret_cast<uint4*>(orow + (o0 + 1) * ostride + w0) = hi;
+                        for (int q = 0; q < 16; ++q) acc[c + q] = v16[q];
                     }
-                } else if (d < p.D && w < p.W) {
+                    tmem_wait_ld();
+                    // The slot is free once read: the MMA warp restarts it with
+                    // accumulate = 0 (no zeroing here).
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_addr(&acc_empty[m]));
 #pragma unroll
                     for (int k = 0; k < COUTP / 2; ++k) {
-                        const __half2 h2 = *reinterpret_cast<const __half2*>(&ph[k]);
-                        if (2 * k < p.Cout) orow[(2 * k) * ostride + w] = __low2half(h2);
-                        if (2 * k + 1 < p.Cout) orow[(2 * k + 1) * ostride + w] = __high2half(h2);
+                        const float2 bb = *reinterpret_cast<const float2*>(sbias + 2 * k);
+                        const __half2 h2 = __floats2half2_rn(act_apply(__uint_as_float(acc[2 * k]) + bb.x, p.act),
+                                                             act_apply(__uint_as_float(acc[2 * k + 1]) + bb.y, p.act));
+                        ph[j][k] = *reinterpret_cast<const uint32_t*>(&h2);
+                    }
+                }
+                if (!ok || r < r0 || r >= r1) continue;  // warp-uniform
+                __half* orow0 = p.out + (i64(b) * p.Cout * p.D) * plane_out + i64(r - p.out_row0) * p.W;
+#pragma unroll
+                for (int j = 0; j < kDrain; ++j) {
+                    if (j >= mcnt) break;
+                    const int d = (m0 + j) * 16 + dsub;
+                    __half* orow = orow0 + i64(d) * plane_out;
+                    if (p.out_vec) {
+                        // The 8 lanes of a lane group hold the 8 columns of one
+                        // disparity: transpose blocks of 8 o-pairs among them so
+                        // each lane ends with 8 columns of two channels, written
+                        // as two 16-byte rows.
+#pragma unroll
+                        for (int blk = 0; blk < COUTP / 16; ++blk) {
+                            uint32_t e[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) e[i] = ph[j][8 * blk + i];
+                            transpose8x8(e, lane);
+                            const int o0 = 16 * blk + 2 * (lane & 7);
+                            const uint4 lo =
+                                make_uint4(__byte_perm(e[0], e[1], 0x5410), __byte_perm(e[2], e[3], 0x5410),
+                                           __byte_perm(e[4], e[5], 0x5410), __byte_perm(e[6], e[7], 0x5410));
+                            const uint4 hi =
+                                make_uint4(__byte_perm(e[0], e[1], 0x7632), __byte_perm(e[2], e[3], 0x7632),
+                                           __byte_perm(e[4], e[5], 0x7632), __byte_perm(e[6], e[7], 0x7632));
+                            if (d < p.D && o0 < p.Cout) *reinterpret_cast<uint4*>(orow + o0 * ostride + w0) = lo;
+                            if (d < p.D && o0 + 1 < p.Cout)
+                                *reinterpret_cast<uint4*>(orow + (o0 + 1) * ostride + w0) = hi;
+                        }
+                    } else if (d < p.D && w < p.W) {
+#pragma unroll
+                        for (int k = 0; k < COUTP / 2; ++k) {
+                            const __half2 h2 = *reinterpret_cast<const __half2*>(&ph[j][k]);
+                            if (2 * k < p.Cout) orow[(2 * k) * ostride + w] = __low2half(h2);
+                            if (2 * k + 1 < p.Cout) orow[(2 * k + 1) * ostride + w] = __high2half(h2);
+                        }
                     }
                 }
             }
@@ -637,6 +646,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         // per-MMA bookkeeping, halve to quarter the issue rate (measured).
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(128, N);
+            constexpr uint32_t idesc1 = idesc_f16_f32(128, COUTP);      // one slot
+            constexpr uint32_t idesc2 = idesc_f16_f32(128, 2 * COUTP);  // two adjacent slots
             const int S = p.nsteps;
             const uint64_t vol_base = smem_addr(sVol) >> 4;
             const uint64_t b_base = smem_addr(sB) >> 4;
@@ -653,7 +664,26 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     const int rot = (((1 - u) % 3) + 3) % 3;
                     const uint64_t a0 = vol_base + static_cast<uint64_t>(((it & 1) * p.vol_buf_bytes) >> 4);
                     const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
-                    for (int st = 0; st < S; ++st) {
+                    // K-step 0 starts output row u+1 in its slot (u+1) mod 3: that
+                    // slot is written with accumulate = 0 (it still holds the row
+                    // the epilogue drained), the other two slots accumulate.
+                    const int sn = (u + 1) % 3;
+                    {
+                        const uint64_t a = p.tmplA[0] + a0, bd = p.tmplB[0] + b0;
+                        constexpr uint64_t blk = (COUTP * 16) >> 4;  // one slot of B rows
+                        for (int m = 0; m < p.n_mb; ++m) {
+                            const uint32_t d = tmem_base + m * N;
+                            const uint64_t am = a + m * mb_step;
+                            mma_f16_ss(d + sn * COUTP, am, bd + sn * blk, idesc1, 0);
+                            if (sn == 0) mma_f16_ss(d + COUTP, am, bd + blk, idesc2, 1);
+                            else if (sn == 2) mma_f16_ss(d, am, bd, idesc2, 1);
+                            else {
+                                mma_f16_ss(d, am, bd, idesc1, 1);
+                                mma_f16_ss(d + 2 * COUTP, am, bd + 2 * blk, idesc1, 1);
+                            }
+                        }
+                    }
+                    for (int st = 1; st < S; ++st) {
                         const uint64_t a = p.tmplA[st] + a0, bd = p.tmplB[st] + b0;
                         for (int m = 0; m < p.n_mb; ++m)
                             mma_f16_ss(tmem_base + m * N, a + m * mb_step, bd, idesc, 1);
@@ -775,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         for (int h = ((pw - job * p.tpj) % kProdWarps + kProdWarps) % kProdWarps; h < p.tpj;
                              h += kProdWarps) {
                             const int jt0 = (h * p.n_tiles) / p.tpj, jt1 = ((h + 1) * p.n_tiles) / p.tpj;
-                            corr_task<CORR, DIV>(p, sbase, zero_row, vsa, jt0, jt1, lane);
+                            corr_task<CORR>(p, sbase, zero_row, vsa, jt0, jt1, lane);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
@@ -877,7 +907,10 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.in_row0 = in_row0; p.in_rows = in_rows; p.out_row0 = out_row0; p.out_rows = out_rows;
     p.Cg = Cg; p.KG = KG; p.Dp = Dp; p.n_mb = n_mb; p.nsteps = nsteps;
     p.n_wtiles = (W + kWt - 1) / kWt;
-    p.scale_div = fused ? corr_scale_div_grouped(true, B, C, G, H, W, D, dev.sm_count) : 0;
+    // The fused correlation scales by * (1 / Cg): exactly / Cg when Cg is a
+    // power of two, within one fp32 ulp of it otherwise (the tensor-core sums
+    // already differ from CorrVolume's fp32 chain at that level), and without
+    // a division subroutine per value.
     p.inv_cg = 1.0f / static_cast<float>(Cg);
     p.vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
                (reinterpret_cast<uintptr_t>(right) % 16 == 0);
@@ -902,6 +935,9 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((5 + 2 * ns + 2 * n_mb) * 8 + 16); };
     p.off_bar = off;
     off += bar_bytes(kMaxSlots);
+    off = (off + 15) & ~15u;
+    p.off_bias = off;
+    off += static_cast<uint32_t>(coutp) * 4;
     off = (off + 1023) & ~1023u;
     p.off_stage = off;
     p.n_tiles = (D + 7) / 8 + 2;
@@ -934,9 +970,15 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                     encode_feature_map(&p.tmap_r, right, B, C, in_rows, W, 64, 8 * Cg, true);
     }
 
-    // Descriptor templates (base address 0; the kernel adds its buffer bases).
+    // Descriptor templates (base address 0; the kernel adds its buffer bases)
+    // and the B image's per-chunk weight offsets.
     for (int s = 0; s < nsteps; ++s) {
         const StepInfo si = step_info(s, KG);
+        for (int c = 0; c < 2; ++c) {
+            const int tap = c ? si.t1 : si.t0, kg = c ? si.kg1 : si.kg0;
+            p.step_off[2 * s + c] = tap < 0 ? -1 : 8 * kg * 27 + (tap / 3) * 9 + (tap % 3);
+            p.step_gv[2 * s + c] = std::min(8, G - 8 * kg);
+        }
         const uint32_t off0 = si.kg0 * p.lbo_vol + tap_shift(si.t0);
         const uint32_t off1 = si.t1 >= 0 ? si.kg1 * p.lbo_vol + tap_shift(si.t1) : off0 + 16;
         p.tmplA[s] = host_smem_desc(off0, off1 - off0, kWtp * 16);
@@ -968,12 +1010,10 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
         kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
         return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
     };
-    if (!fused) return coutp == 16 ? launch(stem_tc_kernel<16, false, 0, false>) : launch(stem_tc_kernel<32, false, 0, false>);
+    if (!fused) return coutp == 16 ? launch(stem_tc_kernel<16, false, 0>) : launch(stem_tc_kernel<32, false, 0>);
     const int cv = corr_variant(Cg);
-    const bool dv = p.scale_div != 0;
-#define WW_FUSED_CASE(CP, CV)                                                                              \
-    if (coutp == CP && cv == CV)                                                                           \
-        return dv ? launch(stem_tc_kernel<CP, true, CV, true>) : launch(stem_tc_kernel<CP, true, CV, false>);
+#define WW_FUSED_CASE(CP, CV) \
+    if (coutp == CP && cv == CV) return launch(stem_tc_kernel<CP, true, CV>);
     WW_FUSED_CASE(16, 1) WW_FUSED_CASE(16, 2) WW_FUSED_CASE(16, 3) WW_FUSED_CASE(16, 4) WW_FUSED_CASE(16, 5)
     WW_FUSED_CASE(32, 1) WW_FUSED_CASE(32, 2) WW_FUSED_CASE(32, 3) WW_FUSED_CASE(32, 4) WW_FUSED_CASE(32, 5)
 #undef WW_FUSED_CASE

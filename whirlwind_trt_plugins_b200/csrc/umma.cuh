@@ -256,8 +256,11 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t saddr, uint32_t pari
 // kWaitRounds suspended polls of <= 1 ms each (seconds in total, orders of
 // magnitude above any legitimate wait in these kernels).
 constexpr uint32_t kWaitRounds = 4000;
+constexpr uint32_t kSpinPolls = 64;  // non-blocking polls before suspending (short waits wake faster)
 __device__ __forceinline__ bool mbar_wait(uint32_t saddr, uint32_t parity)
 {
+    for (uint32_t i = 0; i < kSpinPolls; ++i)
+        if (mbar_test_wait(saddr, parity)) return true;
     for (uint32_t i = 0; i < kWaitRounds; ++i)
         if (mbar_try_wait_hint(saddr, parity, 1000000u)) return true;
     return false;

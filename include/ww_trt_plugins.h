@@ -26,7 +26,7 @@
  *
  * Status codes: 0 on success.  The plugin-level ww_plugin_*_enqueue calls
  * return exactly what IPluginV3OneRuntime::enqueue returns in the reference
- * (0 success, 1 failure; corr_volume.cpp:150-177).  The kernel-level calls
+ * (0 success, 1 failure; corr_volume.cpp:84-111).  The kernel-level calls
  * return a ww_status_t; on a CUDA launch failure they print
  * "[ww_trt_plugins] <function>: CUDA launch failed: <reason>" to stderr, as
  * the reference's lastLaunchError does (src/common/cuda_check.hpp:15-23).
@@ -106,9 +106,14 @@ int ww_cost_stem3d(const void* vol, const void* w, const void* b, void* out,
 
 /* ---------------------------------------------------------------------------
  * Fused CorrVolume -> CostStem3D (extension, "CorrCostStem3D"):
- *   vol = ww_corr_volume(left, right, G groups, D disparities)   (fp16, never stored)
+ *   vol = group-wise correlation of left and right (G groups, D disparities)
  *   out = ww_cost_stem3d(vol, w, b, act)                          [B, Cout, D, H, W]
  * left, right [B, C, H, W] fp16; w [Cout, G, 3, 3, 3] fp16; b [Cout] fp16.
+ * The volume stays in shared memory (fp16, never written to device memory).
+ * It is accumulated on the tensor cores in fp32 and scaled by 1/(C/G), so it
+ * may differ from ww_corr_volume's in the last fp32 bits (and, after fp16
+ * rounding, by one fp16 ulp on rare values); the output agrees with
+ * ww_corr_volume followed by ww_cost_stem3d to within 2e-2 absolute.
  * ------------------------------------------------------------------------- */
 int ww_corr_cost_stem3d(const void* left, const void* right, const void* w, const void* b,
                         void* out, int B, int C, int G, int H, int W, int D, int Cout,
@@ -151,13 +156,13 @@ int ww_plugin_get_int_field(int nb_fields, const char* const* names, const int32
 
 /* "CorrVolume" v"1": field max_disp (default 48) and extension field
  * num_groups (default 1).  Output [B, max_disp, H, W] (num_groups == 1) or
- * [B, num_groups, max_disp, H, W].  corr_volume.cpp:94-148. */
+ * [B, num_groups, max_disp, H, W].  corr_volume.cpp:28-82, 113-139. */
 int ww_plugin_corr_volume_output_dtype(int nb_inputs, const int32_t* in_dtypes, int32_t* out_dtype);
 int ww_plugin_corr_volume_output_dims(int max_disp, int num_groups, int nb_inputs,
                                       const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out);
 int ww_plugin_corr_volume_supports_format(int pos, const ww_tensor_desc_t* in_out,
                                           int nb_inputs, int nb_outputs);
-/* corr_volume.cpp:150-177: 0 on success, 1 on bad rank, dtype or launch. */
+/* corr_volume.cpp:84-111: 0 on success, 1 on bad rank, dtype or launch. */
 int ww_plugin_corr_volume_enqueue(int max_disp, int num_groups, const ww_tensor_desc_t* in_desc,
                                   const void* const* inputs, void* const* outputs, void* stream);
 

@@ -113,9 +113,9 @@ def test_corr_volume_enqueue_rejects_before_launch(ww):
     L = ww.lib()
     ptrs = (ctypes.c_void_p * 2)(None, None)
     outs = (ctypes.c_void_p * 1)(None)
-    # wrong rank -> 1 (corr_volume.cpp:159)
+    # wrong rank -> 1 (corr_volume.cpp:93)
     assert L.ww_plugin_corr_volume_enqueue(24, 1, descs(desc([2, 32, 60])), ptrs, outs, None) == 1
-    # unsupported dtype -> 1 (corr_volume.cpp:175)
+    # unsupported dtype -> 1 (corr_volume.cpp:109)
     assert L.ww_plugin_corr_volume_enqueue(24, 1, descs(desc([1, 8, 4, 8], dtype=2)), ptrs, outs, None) == 1
     # null pointers -> 1
     assert L.ww_plugin_corr_volume_enqueue(24, 1, descs(desc([1, 8, 4, 8])), ptrs, outs, None) == 1

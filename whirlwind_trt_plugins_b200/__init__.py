@@ -18,7 +18,8 @@ reference project):
 * ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
 
 The plugin-level classes mirroring the reference's IPluginV3 plugins live in
-``whirlwind_trt_plugins_b200.plugins``.
+``whirlwind_trt_plugins_b200.plugins``; row-band sharding over several GPUs in
+``whirlwind_trt_plugins_b200.shard``.
 """
 from __future__ import annotations
 

@@ -49,7 +49,8 @@ int current_device_info(DeviceInfo* out) noexcept
         d.cc_minor = minor;
     }
     *out = d;
-    return WW_SUCCESS;
+    // The kernels are built for sm_100a only, which runs on compute capability 10.0.
+    return (d.cc_major == 10 && d.cc_minor == 0) ? WW_SUCCESS : WW_ERR_DEVICE;
 }
 
 int* device_error_slot() noexcept

@@ -155,6 +155,8 @@ int cost_stem3d_ref3_launch(const void* in, void* out, const void* w0, const voi
     if (B == 0 || D == 0 || H == 0 || W == 0) return WW_SUCCESS;
     const int n_dtiles = (D + TD - 1) / TD;
     if (static_cast<long long>(B) * n_dtiles > 65535 || (H + TH - 1) / TH > 65535) return WW_ERR_UNSUPPORTED;
+    DeviceInfo dev;
+    if (current_device_info(&dev) != WW_SUCCESS) return WW_ERR_DEVICE;
     dim3 grid((W + TW - 1) / TW, (H + TH - 1) / TH, B * n_dtiles);
     auto h = [](const void* p) { return static_cast<const __half*>(p); };
     cost_stem3d_ref3_kernel<<<grid, kThreads, 0, stream>>>(h(in), static_cast<__half*>(out), h(w0), h(b0),

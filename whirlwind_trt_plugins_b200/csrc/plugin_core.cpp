@@ -35,7 +35,7 @@ int ww_plugin_get_int_field(int nb_fields, const char* const* names, const int32
 
 // ---------------------------------------------------------------- CorrVolume
 
-// corr_volume.cpp:94-103: output type = input 0 type.
+// corr_volume.cpp:28-37: output type = input 0 type.
 int ww_plugin_corr_volume_output_dtype(int nb_inputs, const int32_t* in_dtypes, int32_t* out_dtype)
 {
     if (nb_inputs < 1 || in_dtypes == nullptr || out_dtype == nullptr) return 1;
@@ -43,7 +43,7 @@ int ww_plugin_corr_volume_output_dtype(int nb_inputs, const int32_t* in_dtypes, 
     return 0;
 }
 
-// corr_volume.cpp:105-124: [B, max_disp, H, W]; with the num_groups extension
+// corr_volume.cpp:39-58: [B, max_disp, H, W]; with the num_groups extension
 // and G > 1: [B, G, max_disp, H, W].
 int ww_plugin_corr_volume_output_dims(int max_disp, int num_groups, int nb_inputs,
                                       const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
@@ -69,7 +69,7 @@ int ww_plugin_corr_volume_output_dims(int max_disp, int num_groups, int nb_input
     return 0;
 }
 
-// corr_volume.cpp:126-148: LINEAR only; position 0 fp16 only (advertising
+// corr_volume.cpp:60-82: LINEAR only; position 0 fp16 only (advertising
 // fp32 would let TensorRT insert a reformat in front of the fast path); the
 // other input and the output must match position 0.
 int ww_plugin_corr_volume_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
@@ -83,7 +83,7 @@ int ww_plugin_corr_volume_supports_format(int pos, const ww_tensor_desc_t* in_ou
     return d.dtype == in_out[0].dtype;
 }
 
-// corr_volume.cpp:150-177: rank-4 input, fp16 or fp32, launch; 0 or 1.
+// corr_volume.cpp:84-111: rank-4 input, fp16 or fp32, launch; 0 or 1.
 int ww_plugin_corr_volume_enqueue(int max_disp, int num_groups, const ww_tensor_desc_t* in_desc,
                                   const void* const* inputs, void* const* outputs, void* stream)
 {

@@ -15,8 +15,9 @@
 //
 //   loader (1 warp)     stages, per group octet ("job"), the left columns
 //                       [w0-8, w0+16) and right columns [w0-8*ceil(D/8), w0+16)
-//                       of the octet's channels into a ring of 2..4 slots with
-//                       16-byte cp.async copies (zero fill outside the image);
+//                       of the octet's channels into a ring of 2..8 slots with
+//                       TMA box copies (16-byte cp.async copies when the
+//                       features do not suit TMA; zero fill outside the image);
 //                       completion is counted on an mbarrier.
 //   producers (8 warps) compute the octet's correlation (fused mode) on the
 //                       warp-level tensor cores (mma.sync, fp32 accumulation;
@@ -44,14 +45,15 @@
 // Measured facts that shape this (B200): an M=128 SS tcgen05.mma costs
 // max(N/2, (4096 + 32 N)/128) cycles (shared-memory read bound below N=128),
 // so N = 3*Cout = 96 runs at ~86 % of peak where N = Cout would run at 40 %;
-// MMAs accumulating into the same columns back to back cost ~93 cycles each,
-// so the MMA warp interleaves two accumulator chains; descriptors come from
-// kernel parameters (constant bank, uniform registers), never from shared
-// memory, so the issue path does not queue behind the producers' loads.
+// MMAs accumulating into the same columns back to back cost ~150 cycles each,
+// so one thread issues a row's MMAs with the M-blocks interleaved inside each
+// K-step; descriptors come from kernel parameters (constant bank, uniform
+// registers), never from shared memory, so the issue path does not queue
+// behind the producers' loads.
 //
 // Synchronisation (mbarriers, every wait bounded):
-//   stage_full[ns]  loader (cp.async completion) -> producers
-//   stage_empty[ns] producers (one arrival per task) -> loader
+//   stage_full[ns]  loader (TMA bytes or cp.async completion) -> producers
+//   stage_empty[ns] producers (one arrival per warp and job) -> loader
 //   vol_full[2]     producers -> MMA        volume buffer ready
 //   vol_empty[2]    MMA (commit) -> producers   all MMAs reading it finished
 //   acc_full[m]     MMA (commit) -> epilogue    row u-1 of M-block m complete
@@ -434,7 +436,6 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     const int r1 = min(r0 + p.strip, p.out_row0 + p.out_rows);     // one past last
     const int u_first = r0 - 1;
     const int n_iter = (r1 - r0) + 2;                              // volume rows u_first .. r1
-    const int Dtp = p.Dp + 2;
     // volume rows inside the image (a contiguous range) and the staging jobs over them
     const int uv0 = max(u_first, 0);
     const int uv1 = min(u_first + n_iter, p.H);

@@ -54,8 +54,11 @@
 // Synchronisation (mbarriers, every wait bounded):
 //   stage_full[ns]  loader (TMA bytes or cp.async completion) -> producers
 //   stage_empty[ns] producers (one arrival per warp and job) -> loader
-//   vol_full[2]     producers -> MMA        volume buffer ready
-//   vol_empty[2]    MMA (commit) -> producers   all MMAs reading it finished
+//   vol_full[nv]    producers -> MMA        volume buffer ready
+//   vol_empty[nv]   MMA (commit) -> producers   all MMAs reading it finished
+// (nv = 2 or 3 volume buffers: with three, the producers run up to two rows
+// ahead of the MMA warp, which hides the rows they produce while the tensor
+// core's operand reads hold the shared memory.)
 //   acc_full[m]     MMA (commit) -> epilogue    row u-1 of M-block m complete
 //   acc_empty[m]    epilogue -> MMA             row u-1's slot read out
 // A wait that expires records an error code in the device error word; the
@@ -88,6 +91,7 @@ constexpr int kLStageW = 24;       // staged left columns [w0-8, w0+16)
 constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
+constexpr int kMaxVBuf = 3;        // volume row buffers
 constexpr int kDrain = 3;          // M-blocks the epilogue drains before storing them
 
 struct StemParams {
@@ -105,6 +109,7 @@ struct StemParams {
     int vec_ok;
     int rstage_w;             // staged right columns
     int n_slots;              // staging ring depth (2..kMaxSlots)
+    int n_vbuf;               // volume row buffers (2..kMaxVBuf)
     int n_tiles;              // 8-column right tiles per job: ceil(D/8) + 2
     int tpj;                  // producer tasks per job (each a range of right tiles)
     int raw_w_smem;           // 1: weights are staged through shared memory at set-up
@@ -221,10 +226,32 @@ __device__ __forceinline__ void transpose8x8(uint32_t (&e)[8], int lane)
     }
 }
 
+// Volume column w' held by row `row` of the correlation tiles: rows 0..7 are
+// w' = 1..8 (the 16-byte aligned staged left columns 8..15, read with
+// ldmatrix), row 8 is w' = 0, row 9 is w' = 9; rows 10..15 are padding.
+__device__ __forceinline__ int tile_row_wp(int row)
+{
+    return row < 8 ? row + 1 : (row == 8 ? 0 : (row == 9 ? 9 : kWtp));
+}
+
+// (x * s, y * s) with one packed fp32 multiply (each lane rounded as
+// __fmul_rn), converted to a half2 (x in the low half).
+__device__ __forceinline__ uint32_t scale_to_half2(float x, float y, float s)
+{
+    uint64_t v, sv, r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(x), "f"(y));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(sv) : "f"(s));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(v), "l"(sv));
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+    const __half2 h2 = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h2);
+}
+
 // Scale, round and store one 16x8 tile of correlation accumulators (8 groups
 // per slot) into the volume buffer vsa ([d' = d+1][w'][8 groups] rows).
 // Accumulator slot s of thread t is row m + 8 (s >> 1) (volume column
-// w' = m + 8 (s >> 1)), column 2q + (s & 1) of right tile jt (staged right
+// w' = tile_row_wp(row)), column 2q + (s & 1) of right tile jt (staged right
 // index 8 jt + 2q + (s & 1)), i.e. disparity d = 8 ceil(D/8) - 1 + w' - index.
 //
 // Lanes with q >= 2 visit the two slots of a pair in the opposite order:
@@ -239,7 +266,7 @@ __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float
     const float inv_cg = p.inv_cg;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int wp = m + 8 * (i >> 1);
+        const int wp = tile_row_wp(m + 8 * (i >> 1));
         const int d = dbase + wp - (8 * jt + 2 * q + ((i & 1) ^ (flip ? 1 : 0)));
         if (wp < kWtp && d >= 0 && d < p.D) {
             uint32_t h[4];
@@ -247,10 +274,7 @@ __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float
             for (int k = 0; k < 4; ++k) {
                 const float a0 = flip ? acc[2 * k][i ^ 1] : acc[2 * k][i];
                 const float a1 = flip ? acc[2 * k + 1][i ^ 1] : acc[2 * k + 1][i];
-                const float v0 = __fmul_rn(a0, inv_cg);
-                const float v1 = __fmul_rn(a1, inv_cg);
-                const __half2 h2 = __floats2half2_rn(v0, v1);
-                h[k] = *reinterpret_cast<const uint32_t*>(&h2);
+                h[k] = scale_to_half2(a0, a1, inv_cg);
             }
             st_shared_v4(vsa + static_cast<uint32_t>(((d + 1) * kWtp + wp) * 16), h[0], h[1], h[2], h[3]);
         }
@@ -299,18 +323,40 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
     const int Cg = p.Cg;
     const uint32_t lslot = slot + p.off_l;
 
-    // A fragments: rows m (w' = m) and m + 8 (w' = m + 8) of the left block;
-    // the staged left index of w' is w' + 7.
+    // A fragments (rows = volume columns, see tile_row_wp; k = channels).
+    // Rows 0..7 are the aligned staged left columns 8..15: one transposing
+    // ldmatrix per 8x8 (group, channel half) matrix, absent channels reading
+    // the zero row.  Rows 8 and 9 (staged columns 7 and 16) are loaded by the
+    // lanes that hold them; rows 10..15 are zero.
     uint32_t a[8][NA];
+    {
+        const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+        for (int j = 0; j < NA * 2; ++j) {  // KM 8: 2 loads of 4 groups; KM 16: 4 loads of 2 groups x 2 halves
+            const int e = KM == 8 ? 4 * j + mi : 2 * j + (mi >> 1);
+            const int c = KM == 8 ? rr : 8 * (mi & 1) + rr;
+            const uint32_t addr = (FULL || c < Cg)
+                                      ? lslot + static_cast<uint32_t>((e * Cg + c) * kLRowBytes + 16)
+                                      : zero_row;
+            uint32_t r4[4];
+            ldmatrix_x4_trans(addr, r4);
 #pragma unroll
-        for (int r = 0; r < NA; ++r) {
-            const int c0 = 2 * q + 8 * (r >> 1);
-            const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * (m + 7 + 8 * (r & 1)));
-            const unsigned short lo = (FULL || c0 < Cg) ? ld_shared_u16(la) : 0;
-            const unsigned short hi = (FULL || c0 + 1 < Cg) ? ld_shared_u16(la + kLRowBytes) : 0;
-            a[e][r] = pack_b16x2(lo, hi);
+            for (int k = 0; k < 4; ++k) {
+                if (KM == 8) a[4 * j + k][0] = r4[k];
+                else a[2 * j + (k >> 1)][2 * (k & 1)] = r4[k];
+            }
+        }
+        const int col = m == 0 ? 7 : 16;  // staged left column of row 8 + m
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+#pragma unroll
+            for (int r = 1; r < NA; r += 2) {
+                const int c0 = 2 * q + 8 * (r >> 1);
+                const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * col);
+                const unsigned short lo = (m < 2 && (FULL || c0 < Cg)) ? ld_shared_u16(la) : 0;
+                const unsigned short hi = (m < 2 && (FULL || c0 + 1 < Cg)) ? ld_shared_u16(la + kLRowBytes) : 0;
+                a[e][r] = pack_b16x2(lo, hi);
+            }
         }
     }
 
@@ -389,11 +435,14 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                 uint32_t a[4];
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
+                    // row m (r even) or 8 + m (r odd) of the tile: see tile_row_wp
                     const int c0 = kc + 2 * q + 8 * (r >> 1);
-                    const uint32_t la =
-                        lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * (m + 7 + 8 * (r & 1)));
-                    const unsigned short lo = c0 < Cg ? ld_shared_u16(la) : 0;
-                    const unsigned short hi = c0 + 1 < Cg ? ld_shared_u16(la + kLRowBytes) : 0;
+                    const bool top = (r & 1) == 0;
+                    const int col = top ? m + 8 : (m == 0 ? 7 : 16);
+                    const bool row_ok = top || m < 2;
+                    const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * col);
+                    const unsigned short lo = (row_ok && c0 < Cg) ? ld_shared_u16(la) : 0;
+                    const unsigned short hi = (row_ok && c0 + 1 < Cg) ? ld_shared_u16(la + kLRowBytes) : 0;
                     a[r] = pack_b16x2(lo, hi);
                 }
                 mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
@@ -505,10 +554,11 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     uint8_t* sB = smem + p.off_b;
     uint8_t* sVol = smem + p.off_vol;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-    uint64_t* vol_full = bars;             // [2]
-    uint64_t* vol_empty = bars + 2;        // [2]
-    uint64_t* final_bar = bars + 4;
-    uint64_t* stage_full = bars + 5;                  // [n_slots]
+    const int NV = p.n_vbuf;
+    uint64_t* vol_full = bars;                        // [NV]
+    uint64_t* vol_empty = bars + kMaxVBuf;            // [NV]
+    uint64_t* final_bar = bars + 2 * kMaxVBuf;
+    uint64_t* stage_full = final_bar + 1;             // [n_slots]
     uint64_t* stage_empty = stage_full + p.n_slots;   // [n_slots]
     uint64_t* acc_full = stage_empty + p.n_slots;     // [n_mb]
     uint64_t* acc_empty = acc_full + p.n_mb;          // [n_mb]
@@ -516,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
 
     // ---- set-up: barriers, TMEM, B image, zeroed volume buffers ----
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NV; ++i) {
             mbar_init(smem_addr(&vol_full[i]), kProdWarps);
             mbar_init(smem_addr(&vol_empty[i]), 1);
         }
@@ -581,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     __syncthreads();  // the staged weights are consumed before the region is zeroed
     // Both volume buffers start as zeros: halo planes and padding stay zero;
     // so do the zero rows that stand in for absent channels.
-    for (uint32_t i = threadIdx.x * 16; i < 2 * p.vol_buf_bytes; i += kThreads * 16)
+    for (uint32_t i = threadIdx.x * 16; i < NV * p.vol_buf_bytes; i += kThreads * 16)
         *reinterpret_cast<uint4*>(sVol + i) = make_uint4(0, 0, 0, 0);
     for (uint32_t i = threadIdx.x * 16; i < 128u; i += kThreads * 16)
         *reinterpret_cast<uint4*>(smem + p.off_zero + i) = make_uint4(0, 0, 0, 0);
@@ -710,7 +760,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             const uint64_t vol_base = smem_addr(sVol) >> 4;
             const uint64_t b_base = smem_addr(sB) >> 4;
             for (int it = 0; it < n_iter; ++it) {
-                if (!wait_or_fail(smem_addr(&vol_full[it & 1]), (it >> 1) & 1, p.err, 2)) break;
+                const int vb = it % NV;
+                if (!wait_or_fail(smem_addr(&vol_full[vb]), (it / NV) & 1, p.err, 2)) break;
                 bool ok = true;
                 for (int m = 0; m < p.n_mb && it > 0 && ok; ++m)
                     ok = wait_or_fail(smem_addr(&acc_empty[m]), (it - 1) & 1, p.err, 3);
@@ -719,14 +770,14 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                 const int u = u_first + it;
                 if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
                     const int rot = (((1 - u) % 3) + 3) % 3;
-                    const uint64_t a0 = vol_base + static_cast<uint64_t>(((it & 1) * p.vol_buf_bytes) >> 4);
+                    const uint64_t a0 = vol_base + static_cast<uint64_t>((vb * p.vol_buf_bytes) >> 4);
                     const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
                     // K-step 0 starts output row u+1 in its slot (u+1) mod 3 (it
                     // still holds the row the epilogue drained).
                     issue_row_n<COUTP>(p, tmem_base, a0, b0, (u + 1) % 3);
                 }
                 for (int m = 0; m < p.n_mb; ++m) mma_commit(smem_addr(&acc_full[m]));
-                mma_commit(smem_addr(&vol_empty[it & 1]));
+                mma_commit(smem_addr(&vol_empty[vb]));
             }
         }
         __syncwarp();
@@ -822,8 +873,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         bool ok = true;
         for (int it = 0; it < n_iter && ok; ++it) {
             const int u = u_first + it;
-            const int vb = it & 1;
-            if (it >= 2 && !warp_wait(smem_addr(&vol_empty[vb]), ((it - 2) >> 1) & 1, p.err, 4)) break;
+            const int vb = it % NV;
+            if (it >= NV && !warp_wait(smem_addr(&vol_empty[vb]), ((it / NV) - 1) & 1, p.err, 4)) break;
             if (u >= 0 && u < p.H) {
                 uint8_t* vbuf = sVol + vb * p.vol_buf_bytes;
                 if (FUSED) {
@@ -953,35 +1004,39 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.rstage_w = 16 + 8 * ((D + 7) / 8);  // right columns [w0 - 8*ceil(D/8), w0 + 16)
     p.tmem_cols = pow2_cols(static_cast<uint32_t>(n_mb * 3 * coutp));
 
-    // shared-memory layout: B image | 2 volume buffers | zero row, barriers |
-    // staging ring (1024-byte aligned slots for the 128-byte TMA swizzle)
-    uint32_t off = 0;
-    p.off_b = off;
-    off += static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
-    off = (off + 127) & ~127u;
-    p.off_vol = off;
+    // shared-memory layout: B image | 2 or 3 volume buffers | zero row,
+    // barriers | staging ring (1024-byte aligned slots for the 128-byte TMA
+    // swizzle).  Three volume buffers when three staging slots still fit.
     p.lbo_vol = static_cast<uint32_t>((Dp + 2) * kWtp * 16);
     // + a zeroed 128-byte guard: the zero-weight partner of a lone octet
     // (step_info, t1 < 0) reads one 16-byte position past the last plane.
     p.vol_buf_bytes = p.lbo_vol * KG + 128;
-    off += 2 * p.vol_buf_bytes;
-    off = (off + 127) & ~127u;
-    p.off_zero = off;
-    off += 128;
-    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((5 + 2 * ns + 2 * n_mb) * 8 + 16); };
-    p.off_bar = off;
-    off += bar_bytes(kMaxSlots);
-    off = (off + 15) & ~15u;
-    p.off_bias = off;
-    off += static_cast<uint32_t>(coutp) * 4;
-    off = (off + 1023) & ~1023u;
-    p.off_stage = off;
     p.n_tiles = (D + 7) / 8 + 2;
     p.n_rbox = (p.rstage_w + 63) / 64;
     p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
     p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
     p.stage_slot_bytes = fused ? ((p.off_l + 8u * Cg * kLRowBytes + 1023) / 1024) * 1024 : 0;
     p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + kLStageW) * 8 * Cg * 2);
+    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 2 * n_mb) * 8 + 16); };
+    auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
+        uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
+        o = (o + 127) & ~127u;
+        p.off_vol = o;
+        o += static_cast<uint32_t>(nv) * p.vol_buf_bytes;
+        o = (o + 127) & ~127u;
+        p.off_zero = o;
+        o += 128;
+        p.off_bar = o;
+        o += bar_bytes(kMaxSlots);
+        o = (o + 15) & ~15u;
+        p.off_bias = o;
+        o += static_cast<uint32_t>(coutp) * 4;
+        return (o + 1023) & ~1023u;
+    };
+    p.n_vbuf = (layout(3) + 3 * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin)) ? 3 : 2;
+    uint32_t off = layout(p.n_vbuf);
+    p.off_b = 0;
+    p.off_stage = off;
     // as many staging slots (2..kMaxSlots) as shared memory holds
     p.n_slots = 2;
     while (fused && p.n_slots < kMaxSlots &&
@@ -1000,7 +1055,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     {
         const size_t wbytes = static_cast<size_t>(Cout) * G * 54;
         p.raw_w_smem = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0) &&
-                       (wbytes <= static_cast<size_t>(2 * p.vol_buf_bytes));
+                       (wbytes <= static_cast<size_t>(p.n_vbuf) * p.vol_buf_bytes);
     }
     p.use_tma = 0;
     if (fused && p.vec_ok && 8 * Cg <= 256) {

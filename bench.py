@@ -46,10 +46,10 @@ UNIT = "voxels/s"
 
 # DRAM bytes (read + write) per launch of the fused kernel, from the ncu
 # captures summarised in profiles/ (None until captured for that config).
-# Config 2: dram__bytes_read.sum 25.12 MB + dram__bytes_write.sum 5.68 MB
+# Config 2: dram__bytes_read.sum 25.78 MB + dram__bytes_write.sum 6.37 MB
 # (profiles/stem_tc_fused_c2_full.md; most of the output is still in L2 when
 # the launch ends, so traffic is below the 83.6 MB of algorithmic bytes).
-NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 30.80e6}
+NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.14e6}
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per step).
 N_E2E_STREAMS = 3

@@ -112,7 +112,7 @@ struct StemParams {
     int n_vbuf;               // volume row buffers (2..kMaxVBuf)
     int n_tiles;              // 8-column right tiles per job: ceil(D/8) + 2
     int tpj;                  // producer tasks per job (each a range of right tiles)
-    int raw_w_smem;           // 1: weights are staged through shared memory at set-up
+    int raw_w_smem;           // weights staged through shared memory at set-up: 2 transposed, 1 as is, 0 not
     int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
     int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
     int n_rbox;               // right boxes of 64 columns per job
@@ -583,29 +583,94 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     }
     if (warp == kMmaWarp) tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
 
-    // Weights [Cout][G][27] fp16.  When aligned, they are first copied into
-    // shared memory (the volume and staging regions, unused until set-up
-    // ends) with coalesced 16-byte copies; the B image is then gathered from
-    // there instead of with scattered 2-byte global loads.
-    const bool wsm = p.raw_w_smem != 0;
-    if (wsm) {
+    // Weights [Cout][G][27] fp16 are first staged into shared memory (the
+    // volume region, unused until set-up ends) and the B image is gathered
+    // from there.  raw_w_smem == 2 (G a multiple of 8): staged transposed to
+    // [Cout][27][G], so the 8 groups of an entry are one aligned 16-byte
+    // load; the lanes of a warp take consecutive (o, g) rows, so their 2-byte
+    // global loads cover one contiguous block and their shared stores are
+    // consecutive halves (no bank conflicts).  raw_w_smem == 1: copied as is
+    // with 16-byte cp.async, gathered with 2-byte loads.  0: gathered from
+    // global memory.
+    const int wmode = p.raw_w_smem;
+    const uint32_t raw = smem_addr(sVol);
+    if (wmode == 2) {
+        const unsigned short* wg = reinterpret_cast<const unsigned short*>(p.w);
+        const int G = p.G;
+        for (int r = threadIdx.x; r < p.Cout * G; r += kThreads) {
+            const int o = r / G, g = r - o * G;
+            const unsigned short* src = wg + static_cast<size_t>(r) * 27;
+            const uint32_t dst = raw + 2u * static_cast<uint32_t>(o * 27 * G + g);
+#pragma unroll
+            for (int t = 0; t < 27; ++t) st_shared_u16(dst + 2u * static_cast<uint32_t>(t * G), __ldg(src + t));
+        }
+        __syncthreads();
+    } else if (wmode == 1) {
         const uint32_t wbytes = static_cast<uint32_t>(p.Cout * p.G * 54);
-        const uint32_t dst0 = smem_addr(sVol);
         for (uint32_t i = threadIdx.x * 16; i < wbytes; i += kThreads * 16)
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n"
                          :
-                         : "r"(dst0 + i), "l"(reinterpret_cast<const uint8_t*>(p.w) + i)
+                         : "r"(raw + i), "l"(reinterpret_cast<const uint8_t*>(p.w) + i)
                          : "memory");
         asm volatile("cp.async.wait_all;\n" ::: "memory");
         __syncthreads();
     }
+    // TMA staging of job j (volume row uv0 + j / KG, group octet j % KG) into
+    // slot j % n_slots: one elected lane arms stage_full with the byte count
+    // and issues n_rbox right boxes and one left box (zero fill outside the
+    // image and past the last channel).
+    const int n_runs = (p.D + 7) / 8;
+    auto tma_job = [&](int j) {
+        const int slot = j % p.n_slots;
+        const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
+        const int urow = uv0 + j / p.KG - p.in_row0;
+        const int c0 = (j % p.KG) * 8 * p.Cg;
+        const uint32_t full = smem_addr(&stage_full[slot]);
+        mbar_arrive_expect_tx(full, p.stage_tx);
+        for (int k = 0; k < p.n_rbox; ++k)
+            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs + 64 * k, urow, c0, b, full);
+        tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, c0, b, full);
+    };
+    // The first n_slots jobs need no free slot: issue them now, so their
+    // loads overlap the B image build (the staging ring is not touched by
+    // set-up; the barriers are initialised and visible after the sync above).
+    const int n_pre = (FUSED && p.use_tma && wmode != 0) ? min(p.n_slots, total_jobs) : 0;
+    if (n_pre > 0 && warp == kLoadWarp) {
+        if (elect_one())
+            for (int j = 0; j < n_pre; ++j) tma_job(j);
+        __syncwarp();
+    }
     // B image: entry (step s, chunk c, row n = blk * COUTP + o) holds the 8
     // fp16 weights of the chunk's group octet for output channel o and tap
     // (kd, kh, kw); blocks blk = 0..4 are [kh2, kh1, kh0, kh2, kh1].  The
-    // host precomputes each chunk's tap offset (step_off; -1 for a
-    // zero-weight partner) and valid group count (step_gv).
-    {
-        const uint32_t raw = smem_addr(sVol);
+    // host precomputes each chunk's tap offset (step_off = 216 kg + 9 kd + kw;
+    // -1 for a zero-weight partner) and valid group count (step_gv).
+    if (wmode == 2) {
+        // One item per (chunk, kh, o): one 16-byte load, stored to the one or
+        // two blocks of that kh.
+        const int G = p.G;
+        for (int i = threadIdx.x; i < p.nsteps * 2 * 3 * COUTP; i += kThreads) {
+            const int o = i % COUTP, r2 = i / COUTP;
+            const int kh = r2 % 3, sc = r2 / 3;
+            const int toff = p.step_off[sc], gv = p.step_gv[sc];
+            uint32_t v[4] = {0u, 0u, 0u, 0u};
+            if (toff >= 0 && o < p.Cout) {
+                const int kg = toff / 216, tap = toff - kg * 216 + kh * 3;
+                ld_shared_v4(raw + 2u * static_cast<uint32_t>((o * 27 + tap) * G + 8 * kg), v);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (2 * q >= gv) v[q] &= 0xFFFF0000u;
+                    if (2 * q + 1 >= gv) v[q] &= 0x0000FFFFu;
+                }
+            }
+            const int blk0 = 2 - kh;  // kh2 -> 0 (and 3), kh1 -> 1 (and 4), kh0 -> 2
+            st_shared_v4(smem_addr(sB) + 16u * static_cast<uint32_t>((sc * 5 + blk0) * COUTP + o), v[0], v[1],
+                         v[2], v[3]);
+            if (kh > 0)
+                st_shared_v4(smem_addr(sB) + 16u * static_cast<uint32_t>((sc * 5 + blk0 + 3) * COUTP + o), v[0],
+                             v[1], v[2], v[3]);
+        }
+    } else {
         const unsigned short* wg = reinterpret_cast<const unsigned short*>(p.w);
         const int g27 = p.G * 27;
         for (int i = threadIdx.x; i < p.nsteps * 2 * NR; i += kThreads) {
@@ -619,8 +684,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                 unsigned short h[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e)
-                    h[e] = e < gv ? (wsm ? ld_shared_u16(raw + 2u * static_cast<uint32_t>(base + e * 27))
-                                         : wg[base + e * 27])
+                    h[e] = e < gv ? (wmode == 1 ? ld_shared_u16(raw + 2u * static_cast<uint32_t>(base + e * 27))
+                                                : wg[base + e * 27])
                                   : static_cast<unsigned short>(0);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) v[q] = pack_b16x2(h[2 * q], h[2 * q + 1]);
@@ -792,29 +857,22 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         if (FUSED) {
             const int Cg = p.Cg;
             const int NS = p.n_slots;
-            const int n_runs = (p.D + 7) / 8;
             const int rbase = w0 - 8 * n_runs;
             const int nvr = p.rstage_w / 8;
-            int issued = 0;
-            for (int j = 0; j < total_jobs; ++j) {
+            int issued = n_pre;  // jobs [0, n_pre) were issued during set-up
+            for (int j = n_pre; j < total_jobs; ++j) {
                 const int slot = j % NS;
                 if (j >= NS && !warp_wait(smem_addr(&stage_empty[slot]), ((j / NS) - 1) & 1, p.err, 6)) break;
                 issued = j + 1;
+                if (p.use_tma) {
+                    if (elect_one()) tma_job(j);
+                    __syncwarp();
+                    continue;
+                }
                 const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
                 const int urow = uv0 + j / p.KG - p.in_row0;
                 const int kg = j % p.KG;
                 const uint32_t full = smem_addr(&stage_full[slot]);
-                if (p.use_tma) {
-                    if (elect_one()) {
-                        mbar_arrive_expect_tx(full, p.stage_tx);
-                        for (int k = 0; k < p.n_rbox; ++k)
-                            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, rbase + 64 * k, urow, kg * 8 * Cg, b,
-                                        full);
-                        tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, kg * 8 * Cg, b, full);
-                    }
-                    __syncwarp();
-                    continue;
-                }
                 for (int lc = lane; lc < 8 * Cg; lc += 32) {  // lc = row of the job (e * Cg + c)
                     const int ge = lc / Cg, cc = lc - ge * Cg;
                     const int g = kg * 8 + ge;
@@ -1054,8 +1112,10 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.out_vec = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     {
         const size_t wbytes = static_cast<size_t>(Cout) * G * 54;
-        p.raw_w_smem = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0) &&
-                       (wbytes <= static_cast<size_t>(p.n_vbuf) * p.vol_buf_bytes);
+        const bool fits = wbytes <= static_cast<size_t>(p.n_vbuf) * p.vol_buf_bytes;
+        p.raw_w_smem = !fits ? 0
+                       : (G % 8 == 0) ? 2
+                       : ((reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0)) ? 1 : 0;
     }
     p.use_tma = 0;
     if (fused && p.vec_ok && 8 * Cg <= 256) {

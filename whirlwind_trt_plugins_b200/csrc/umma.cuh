@@ -346,6 +346,19 @@ __device__ __forceinline__ uint32_t pack_b16x2(unsigned short lo, unsigned short
     return r;
 }
 
+__device__ __forceinline__ void st_shared_u16(uint32_t saddr, unsigned short v)
+{
+    asm volatile("st.shared.u16 [%0], %1;\n" : : "r"(saddr), "h"(v) : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t saddr, uint32_t (&v)[4])
+{
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(saddr)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
 {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" : : "r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d)

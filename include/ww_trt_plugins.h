@@ -14,9 +14,12 @@
  *                             src/plugins/corr_volume/corr_volume_kernel.hpp:17-27
  *   ww_cost_stem3d_ref3       whirlwind::launchCostStem3D
  *                             src/plugins/cost_stem_3d/cost_stem_3d_kernel.hpp:17-30
+ *   ww_nv12_decode            whirlwind::launchNv12Decode<T>
+ *                             src/plugins/nv12_decode/nv12_decode_kernel.hpp:20-28
  *   ww_plugin_*               the IPluginV3 methods of CorrVolumePlugin
  *                             (src/plugins/corr_volume/corr_volume.cpp:28-139) and
  *                             CostStem3DPlugin (src/plugins/cost_stem_3d/cost_stem_3d.cpp:19-97),
+ *                             Nv12DecodePlugin (src/plugins/nv12_decode/nv12_decode.cpp:26-146),
  *                             with TensorRT types replaced by ww_tensor_desc_t
  * Extensions with no reference symbol (group-wise correlation fused with a
  * single G -> Cout 3-D conv stem):
@@ -54,8 +57,8 @@ typedef enum ww_status {
     WW_ERR_DEVICE = 7         /* no usable sm_100 device is current              */
 } ww_status_t;
 
-/* Same numeric values as nvinfer1::DataType::kFLOAT / kHALF. */
-typedef enum ww_dtype { WW_DTYPE_FLOAT = 0, WW_DTYPE_HALF = 1 } ww_dtype_t;
+/* Same numeric values as nvinfer1::DataType::kFLOAT / kHALF / kINT8. */
+typedef enum ww_dtype { WW_DTYPE_FLOAT = 0, WW_DTYPE_HALF = 1, WW_DTYPE_INT8 = 2 } ww_dtype_t;
 
 /* Activation of the generalised / fused stem. */
 typedef enum ww_act { WW_ACT_RELU = 0, WW_ACT_RELU6 = 1 } ww_act_t;
@@ -131,6 +134,19 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
                              int act, int in_row0, int in_rows, int out_row0, int out_rows,
                              void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Nv12Decode: NV12 -> planar RGB in [-1, 1], bilinear resize.
+ * nv12 : [B, H_IN * 3 / 2, W_IN] uint8 (Y plane, then interleaved U/V rows
+ *        at half resolution); out : [B, 3, H_OUT, W_OUT], dtype
+ *        WW_DTYPE_HALF or WW_DTYPE_FLOAT.  align_corners = False sampling
+ *        with clamped taps, full-range BT.601 fused with 2 * (rgb / 255) - 1,
+ *        fp32 arithmetic identical to the reference kernel's.  Every batch
+ *        item is decoded (the reference launcher takes one image).
+ * Replaces whirlwind::launchNv12Decode<T> (nv12_decode_kernel.hpp:20-28).
+ * ------------------------------------------------------------------------- */
+int ww_nv12_decode(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT, int W_OUT,
+                   void* stream);
+
 /* BatchNorm folding on the host: w16[o, :] = fp16(w[o, :] * scale[o]) computed in
  * fp32, b16[o] = fp16(bias[o]); k = Cin * 27.  Host memory only. */
 int ww_fold_bn_f16(const float* w, const float* scale, const float* bias, int cout, int k,
@@ -189,6 +205,18 @@ int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act,
                                        const ww_tensor_desc_t* in_desc,
                                        const void* const* inputs, void* const* outputs,
                                        void* stream);
+
+/* "Nv12Decode" v"1": fields out_h (default 224), out_w (default 288); input
+ * [B, H_IN * 3 / 2, W_IN] declared INT8 (uint8 bytes), output [B, 3, out_h,
+ * out_w] declared FLOAT, built as fp16 or fp32.  nv12_decode.cpp:26-146. */
+int ww_plugin_nv12_decode_output_dtype(int nb_inputs, int32_t* out_dtype);
+int ww_plugin_nv12_decode_output_dims(int out_h, int out_w, int nb_inputs, const ww_tensor_desc_t* inputs,
+                                      ww_tensor_desc_t* out);
+int ww_plugin_nv12_decode_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                          int nb_outputs);
+int ww_plugin_nv12_decode_enqueue(int out_h, int out_w, const ww_tensor_desc_t* in_desc,
+                                  const ww_tensor_desc_t* out_desc, const void* const* inputs,
+                                  void* const* outputs, void* stream);
 
 /* Device error word written by bounded waits inside the tensor-core kernels
  * (0 = none).  Reading it synchronises the current device.  Clearing resets

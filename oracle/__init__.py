@@ -70,6 +70,7 @@ def lib() -> ctypes.CDLL:
         L.orc_f32_to_f16_array.argtypes = [p, p, ctypes.c_int64]
         L.orc_f32_to_f16_array.restype = None
         L.orc_hw_threads.restype = i
+        L.orc_nv12_decode.argtypes = [p] + [i] * 6 + [p, i]
         _lib = L
     return _lib
 
@@ -89,6 +90,8 @@ def ref_lib() -> ctypes.CDLL:
         R.wwref_corr_volume_f32.argtypes = [p, p, p] + [i] * 5 + [p]
         R.wwref_corr_volume_grouped_f16.argtypes = [p, p, p] + [i] * 6 + [p]
         R.wwref_cost_stem3d.argtypes = [p] * 8 + [i] * 4 + [p]
+        R.wwref_nv12_decode_f16.argtypes = [p, p] + [i] * 4 + [p]
+        R.wwref_nv12_decode_f32.argtypes = [p, p] + [i] * 4 + [p]
         _ref = R
     return _ref
 
@@ -219,3 +222,16 @@ def fold_bn(w: np.ndarray, scale: np.ndarray, bias: np.ndarray) -> tuple[np.ndar
     b16 = np.empty((cout,), dtype=np.uint16)
     lib().orc_fold_bn(_ptr(w), _ptr(scale), _ptr(bias), cout, k, _ptr(w16), _ptr(b16))
     return w16.view(np.float16), b16.view(np.float16)
+
+
+def nv12_decode(nv12: np.ndarray, H_OUT: int, W_OUT: int, out_f16: bool = True, nthreads: int = 0) -> np.ndarray:
+    """NV12 [B, H_IN * 3 / 2, W_IN] uint8 -> [B, 3, H_OUT, W_OUT] fp16 (or fp32)."""
+    a = np.ascontiguousarray(nv12, dtype=np.uint8)
+    if a.ndim == 2:
+        a = a[None]
+    B, H_NV12, W_IN = a.shape
+    H_IN = H_NV12 * 2 // 3
+    out = np.empty((B, 3, H_OUT, W_OUT), dtype=np.uint16 if out_f16 else np.float32)
+    _check(lib().orc_nv12_decode(_ptr(a), B, H_IN, W_IN, H_OUT, W_OUT, int(out_f16), _ptr(out), nthreads),
+           "nv12_decode")
+    return out.view(np.float16) if out_f16 else out

@@ -2,8 +2,9 @@
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together
 // with the UNMODIFIED reference kernel sources, read in place from the
-// reference tree (src/plugins/corr_volume/corr_volume_kernel.cu and
-// src/plugins/cost_stem_3d/cost_stem_3d_kernel.cu), into
+// reference tree (src/plugins/corr_volume/corr_volume_kernel.cu,
+// src/plugins/cost_stem_3d/cost_stem_3d_kernel.cu and
+// src/plugins/nv12_decode/nv12_decode_kernel.cu), into
 // oracle/_ref/libww_ref.so.  tests/golden/make_golden.py and the GPU parity
 // tests call it to pin the CPU oracle and the product against the
 // reference's actual results; bench.py may time it for context.  Nothing in
@@ -17,6 +18,7 @@
 
 #include "plugins/corr_volume/corr_volume_kernel.hpp"
 #include "plugins/cost_stem_3d/cost_stem_3d_kernel.hpp"
+#include "plugins/nv12_decode/nv12_decode_kernel.hpp"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -58,6 +60,21 @@ int wwref_corr_volume_grouped_f16(const void* left, const void* right, void* out
             if (e != cudaSuccess) return static_cast<int>(e);
         }
     return 0;
+}
+
+// NV12 decode of one image (the reference launcher takes no batch).
+int wwref_nv12_decode_f16(const void* nv12, void* out, int H_IN, int W_IN, int H_OUT, int W_OUT, void* stream)
+{
+    return static_cast<int>(whirlwind::launchNv12Decode<__half>(static_cast<const uint8_t*>(nv12),
+                                                                 static_cast<__half*>(out), H_IN, W_IN, H_OUT,
+                                                                 W_OUT, static_cast<cudaStream_t>(stream)));
+}
+
+int wwref_nv12_decode_f32(const void* nv12, void* out, int H_IN, int W_IN, int H_OUT, int W_OUT, void* stream)
+{
+    return static_cast<int>(whirlwind::launchNv12Decode<float>(static_cast<const uint8_t*>(nv12),
+                                                                static_cast<float*>(out), H_IN, W_IN, H_OUT,
+                                                                W_OUT, static_cast<cudaStream_t>(stream)));
 }
 
 int wwref_cost_stem3d(const void* in, void* out,

@@ -8,11 +8,11 @@
  * Arithmetic follows the reference kernels operation for operation where
  * the reference defines it:
  *   - correlation: one fp32 fma chain over the channels of a group, in
- *     channel order, starting from +0 (corr_volume_kernel.cu:102-111 and
- *     :235-247; nvcc contracts `acc += a*b` into fma), then either a true
- *     division by C (naive kernel, :113) or a multiply by the host-computed
- *     1.0f/C (fast kernel, :256 with invC from :385), rounded to fp16 RNE;
- *     +0 wherever w - d < 0 (:104 / the zero-staged halo at :205-215).
+ *     channel order, starting from +0 (corr_volume_kernel.cu:73-82 and
+ *     :211-216; nvcc contracts `acc += a*b` into fma), then either a true
+ *     division by C (naive kernel, :84) or a multiply by the host-computed
+ *     1.0f/C (fast kernel, :227 with invC from :356), rounded to fp16 RNE;
+ *     +0 wherever w - d < 0 (:75 / the zero-staged halo at :179-186).
  *   - reference stem: per stage an fma chain in (ci, kd, kh, kw) order,
  *     then + bias, ReLU6, fp16 RNE; positions outside the volume are zero
  *     for the next stage (cost_stem_3d_kernel.cu:115-232).
@@ -149,12 +149,12 @@ static void orc_parallel_for(int64_t n, int nthreads, orc_body_fn fn, void* ctx)
 }
 
 /* ------------------------------------------------------------------ */
-/* Reference kernel selection (corr_volume_kernel.cu:280-397)          */
+/* Reference kernel selection (corr_volume_kernel.cu:251-368)          */
 /* ------------------------------------------------------------------ */
 
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-/* pickTileW, corr_volume_kernel.cu:280-328: full-row tile, split for
+/* pickTileW, corr_volume_kernel.cu:251-312: full-row tile, split for
  * occupancy when H*B < SMs/2, capped by 48 KB of shared memory and 1024
  * threads, rounded to 8, then balanced.                                */
 static int ref_pick_tile(int C, int B, int H, int W, int PADA, int dispY, int sm_count)
@@ -192,7 +192,7 @@ int orc_ref_corr_scale_mode(int is_half, int B, int C, int H, int W, int D, int 
     const int dispY = D / 6;
     const int PADA = round_up(D - 1, 8);
     const int tile = ref_pick_tile(C, B, H, W, PADA, dispY, sm_count);
-    /* fastPathApplies, corr_volume_kernel.cu:343-354 */
+    /* fastPathApplies, corr_volume_kernel.cu:314-326 */
     if (W % 8 != 0) return ORC_SCALE_DIV;
     const long long outputs = (long long)B * D * H * W;
     if (outputs < (long long)sm_count * 800) return ORC_SCALE_DIV;
@@ -299,7 +299,7 @@ static float relu6f(float v) { return fminf(6.0f, fmaxf(0.0f, v)); }
 
 /* One Conv3d 3x3x3 pad-1 stage over fp16-valued float inputs
  * src[cin][D][H][W] -> dst[cout][D][H][W] (rounded to fp16 values),
- * accumulation order (ci, kd, kh, kw) as at cost_stem_3d_kernel.cu:337-350. */
+ * accumulation order (ci, kd, kh, kw) as at cost_stem_3d_kernel.cu:164-179. */
 static void ref3_stage(const float* src, float* dst, const float* wt, const float* bias,
                        int cin, int cout, int D, int H, int W)
 {
@@ -510,4 +510,106 @@ void orc_fold_bn(const float* w, const float* scale, const float* bias,
         for (int i = 0; i < k; ++i) w16[(int64_t)o * k + i] = orc_f32_to_f16(w[(int64_t)o * k + i] * scale[o]);
         b16[o] = orc_f32_to_f16(bias[o]);
     }
+}
+
+/* ------------------------------------------------------------------ */
+/* NV12 -> normalised planar RGB (nv12_decode_kernel.cu:33-188)         */
+/* ------------------------------------------------------------------ */
+/* Per output pixel, in fp32, operation for operation as nvcc compiles the
+ * reference expressions (it contracts a*b + c into one fma; both the CUDA
+ * kernel of this library and this restatement spell the contractions out):
+ *   src = fma(dst + 0.5, scale, -0.5)                       (:130-139)
+ *   bilinear: top = fma(wx0, v00, wx1 * v01), bot likewise,
+ *             val = fma(wy0, top, wy1 * bot)               (:58, :97-98)
+ *   coordinates clamped to the plane after the weights      (:48-51, :78-81)
+ *   R = fma(s, fma(1.402, Cr, Y), -1)
+ *   G = fma(s, fma(-0.714136, Cr, fma(-0.344136, Cb, Y)), -1)
+ *   B = fma(s, fma(1.772, Cb, Y), -1),  s = 2/255, Cb = U - 128, Cr = V - 128
+ *                                                           (:104-113, :143)
+ * The reference launcher covers batch item 0 only (nv12_decode.cpp:96-114
+ * passes no batch to launchNv12Decode); every batch item is computed here. */
+
+static float nv12_bilinear(const uint8_t* plane, int rows, int cols, int row_stride, int step, float yf,
+                           float xf)
+{
+    const int y0 = (int)floorf(yf), x0 = (int)floorf(xf);
+    const float wy1 = yf - (float)y0, wy0 = 1.0f - wy1;
+    const float wx1 = xf - (float)x0, wx0 = 1.0f - wx1;
+    const int y0c = y0 < 0 ? 0 : (y0 > rows - 1 ? rows - 1 : y0);
+    const int y1c = y0 + 1 < 0 ? 0 : (y0 + 1 > rows - 1 ? rows - 1 : y0 + 1);
+    const int x0c = x0 < 0 ? 0 : (x0 > cols - 1 ? cols - 1 : x0);
+    const int x1c = x0 + 1 < 0 ? 0 : (x0 + 1 > cols - 1 ? cols - 1 : x0 + 1);
+    const float v00 = (float)plane[(int64_t)y0c * row_stride + (int64_t)step * x0c];
+    const float v01 = (float)plane[(int64_t)y0c * row_stride + (int64_t)step * x1c];
+    const float v10 = (float)plane[(int64_t)y1c * row_stride + (int64_t)step * x0c];
+    const float v11 = (float)plane[(int64_t)y1c * row_stride + (int64_t)step * x1c];
+    const float top = fmaf(wx0, v00, wx1 * v01);
+    const float bot = fmaf(wx0, v10, wx1 * v11);
+    return fmaf(wy0, top, wy1 * bot);
+}
+
+typedef struct {
+    const uint8_t* nv12;
+    int H_IN, W_IN, H_OUT, W_OUT, out_f16;
+    void* out;
+    float sy_h, sy_w, suv_h, suv_w;
+} nv12_ctx;
+
+static void nv12_body(void* vctx, int64_t item)  /* item = b * H_OUT + y */
+{
+    const nv12_ctx* c = (const nv12_ctx*)vctx;
+    const int b = (int)(item / c->H_OUT), y = (int)(item % c->H_OUT);
+    const int64_t in_img = (int64_t)c->H_IN * 3 / 2 * c->W_IN;
+    const uint8_t* img = c->nv12 + (int64_t)b * in_img;
+    const uint8_t* chroma = img + (int64_t)c->H_IN * c->W_IN;
+    const int H_UV = c->H_IN >> 1, W_UV = c->W_IN >> 1;
+    const int64_t plane = (int64_t)c->H_OUT * c->W_OUT;
+    const float s = 2.0f / 255.0f;
+    const float yf_y = fmaf((float)y + 0.5f, c->sy_h, -0.5f);
+    const float yf_uv = fmaf((float)y + 0.5f, c->suv_h, -0.5f);
+    for (int x = 0; x < c->W_OUT; ++x) {
+        const float xf_y = fmaf((float)x + 0.5f, c->sy_w, -0.5f);
+        const float xf_uv = fmaf((float)x + 0.5f, c->suv_w, -0.5f);
+        const float Y = nv12_bilinear(img, c->H_IN, c->W_IN, c->W_IN, 1, yf_y, xf_y);
+        const float U = nv12_bilinear(chroma, H_UV, W_UV, c->W_IN, 2, yf_uv, xf_uv);
+        const float V = nv12_bilinear(chroma + 1, H_UV, W_UV, c->W_IN, 2, yf_uv, xf_uv);
+        const float Cb = U - 128.0f, Cr = V - 128.0f;
+        const float R = fmaf(s, fmaf(1.402f, Cr, Y), -1.0f);
+        const float G = fmaf(s, fmaf(-0.714136f, Cr, fmaf(-0.344136f, Cb, Y)), -1.0f);
+        const float B = fmaf(s, fmaf(1.772f, Cb, Y), -1.0f);
+        const int64_t o = ((int64_t)b * 3) * plane + (int64_t)y * c->W_OUT + x;
+        if (c->out_f16) {
+            uint16_t* out = (uint16_t*)c->out;
+            out[o] = orc_f32_to_f16(R);
+            out[o + plane] = orc_f32_to_f16(G);
+            out[o + 2 * plane] = orc_f32_to_f16(B);
+        } else {
+            float* out = (float*)c->out;
+            out[o] = R;
+            out[o + plane] = G;
+            out[o + 2 * plane] = B;
+        }
+    }
+}
+
+int orc_nv12_decode(const uint8_t* nv12, int B, int H_IN, int W_IN, int H_OUT, int W_OUT, int out_f16,
+                    void* out, int nthreads)
+{
+    if (nv12 == NULL || out == NULL) return 1;
+    if (B < 0 || H_IN < 2 || W_IN < 2 || H_OUT < 1 || W_OUT < 1) return 2;
+    nv12_ctx c;
+    c.nv12 = nv12;
+    c.H_IN = H_IN;
+    c.W_IN = W_IN;
+    c.H_OUT = H_OUT;
+    c.W_OUT = W_OUT;
+    c.out_f16 = out_f16;
+    c.out = out;
+    /* nv12_decode_kernel.cu:213-216 */
+    c.sy_h = (float)H_IN / (float)H_OUT;
+    c.sy_w = (float)W_IN / (float)W_OUT;
+    c.suv_h = (float)(H_IN >> 1) / (float)H_OUT;
+    c.suv_w = (float)(W_IN >> 1) / (float)W_OUT;
+    orc_parallel_for((int64_t)B * H_OUT, nthreads, nv12_body, &c);
+    return 0;
 }

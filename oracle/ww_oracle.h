@@ -34,13 +34,13 @@ extern "C" {
 
 /* How the channel mean is formed after the fp32 sum (see orc_corr_f16).   */
 enum {
-    ORC_SCALE_DIV = 0,    /* acc / (float)C      corr_volume_kernel.cu:113  */
-    ORC_SCALE_MULINV = 1  /* acc * (1.0f / C)    corr_volume_kernel.cu:256,385 */
+    ORC_SCALE_DIV = 0,    /* acc / (float)C      corr_volume_kernel.cu:84   */
+    ORC_SCALE_MULINV = 1  /* acc * (1.0f / C)    corr_volume_kernel.cu:227,356 */
 };
 
 /* Accumulation mode of the generalised stem. */
 enum {
-    ORC_ACC_F32_SEQ = 0,  /* fmaf in (ci, kd, kh, kw) order, like cost_stem_3d_kernel.cu:337-350 */
+    ORC_ACC_F32_SEQ = 0,  /* fmaf in (ci, kd, kh, kw) order, like cost_stem_3d_kernel.cu:164-179 */
     ORC_ACC_F64 = 1       /* double accumulation, one rounding at the end ("truth") */
 };
 
@@ -53,13 +53,13 @@ void orc_f32_to_f16_array(const float* src, uint16_t* dst, int64_t n);
 void orc_f16_to_f32_array(const uint16_t* src, float* dst, int64_t n);
 
 /* Which of the reference's two CorrVolume kernels launchCorrVolume<__half>
- * would pick for one call (corr_volume_kernel.cu:361-397): returns
+ * would pick for one call (corr_volume_kernel.cu:333-368): returns
  * ORC_SCALE_MULINV when corrVolumeFastKernel runs, ORC_SCALE_DIV when the
  * naive corrVolumeKernel runs.  Restates fastPathApplies/pickTileW
- * (corr_volume_kernel.cu:280-354) for an SM count `sm_count`.          */
+ * (corr_volume_kernel.cu:251-326) for an SM count `sm_count`.          */
 int orc_ref_corr_scale_mode(int is_half, int B, int C, int H, int W, int D, int sm_count);
 
-/* Correlation volume (corr_volume_kernel.cu:80-117 and :146-268), group-wise:
+/* Correlation volume (corr_volume_kernel.cu:52-88 and :118-239), group-wise:
  *   out[b,g,d,h,w] = scale( sum_{c in group g} L[b,c,h,w] * R[b,c,h,w-d] )
  * with the sum a sequential fp32 fma chain over c (what nvcc emits for
  * `acc += a*b`), scale per `scale_mode`, and exact +0 when w-d < 0.
@@ -103,6 +103,14 @@ void orc_fold_bn(const float* w, const float* scale, const float* bias,
                  int cout, int k, uint16_t* w16, uint16_t* b16);
 
 int orc_hw_threads(void);
+
+/* NV12 [B, H_IN * 3 / 2, W_IN] uint8 -> planar RGB [B, 3, H_OUT, W_OUT] in
+ * [-1, 1] (fp16 bit patterns if out_f16, else fp32): bilinear resize with
+ * align_corners = False and clamped taps, full-range BT.601 fused with
+ * 2 * (rgb / 255) - 1 (nv12_decode_kernel.cu:33-188, launcher :197-230).
+ * Every batch item (the reference plugin decodes batch 0 only).         */
+int orc_nv12_decode(const uint8_t* nv12, int B, int H_IN, int W_IN, int H_OUT, int W_OUT, int out_f16,
+                    void* out, int nthreads);
 
 #ifdef __cplusplus
 }

@@ -4,14 +4,16 @@ The reference (IntelligentRoboticsLab/whirlwind_trt_plugins) ships no test
 vectors, so the fixtures are produced by the reference's OWN CUDA kernels:
 ``oracle/_ref/libww_ref.so`` is compiled by ``oracle/Makefile`` from the
 unmodified reference sources (src/plugins/corr_volume/corr_volume_kernel.cu,
-src/plugins/cost_stem_3d/cost_stem_3d_kernel.cu) for sm_100a.  This script
-runs them on a B200 on seeded inputs and saves inputs + outputs as .npz:
+src/plugins/cost_stem_3d/cost_stem_3d_kernel.cu,
+src/plugins/nv12_decode/nv12_decode_kernel.cu) for sm_100a.  This script runs
+them on a B200 on seeded inputs and saves inputs + outputs as .npz:
 
-    python tests/golden/make_golden.py [out_dir]      (needs a GPU)
+    python tests/golden/make_golden.py [out_dir [name_filter]]   (needs a GPU)
 
 Each case calls the reference launcher exactly as the reference plugin does
 (launchCorrVolume<T>(left, right, out, B, C, H, W, D, stream) and
-launchCostStem3D(in, out, w0, b0, w1, b1, w2, b2, B, D, H, W, stream));
+launchCostStem3D(in, out, w0, b0, w1, b1, w2, b2, B, D, H, W, stream) and
+launchNv12Decode<T>(nv12, out, H_IN, W_IN, H_OUT, W_OUT, stream));
 group-wise correlation is the reference called once per (batch, group), the
 only way the reference can produce it.
 """
@@ -42,6 +44,11 @@ CASES = [
     ("stem3_native", "stem3", dict(B=1, D=48, H=32, W=40, seed=21)),
     ("stem3_ragged", "stem3", dict(B=1, D=13, H=9, W=11, seed=22)),
     ("stem3_tiny", "stem3", dict(B=1, D=1, H=1, W=1, seed=23)),
+    ("nv12_16_down2", "nv12_16", dict(H_IN=96, W_IN=128, H_OUT=48, W_OUT=64, seed=24)),
+    ("nv12_16_up_odd", "nv12_16", dict(H_IN=30, W_IN=40, H_OUT=45, W_OUT=61, seed=25)),
+    ("nv12_16_default", "nv12_16", dict(H_IN=120, W_IN=160, H_OUT=224, W_OUT=288, seed=26)),
+    ("nv12_32_default", "nv12_32", dict(H_IN=120, W_IN=160, H_OUT=224, W_OUT=288, seed=27)),
+    ("nv12_32_ragged", "nv12_32", dict(H_IN=14, W_IN=22, H_OUT=9, W_OUT=13, seed=28)),
 ]
 
 
@@ -96,6 +103,19 @@ def run_case(name: str, kind: str, prm: dict) -> dict:
         torch.cuda.synchronize()
         assert rc == 0, f"{name}: reference launcher returned {rc}"
         out.update(vol=x, out=to.cpu().numpy(), B=B, D=D, H=H, W=W, **ws)
+    elif kind in ("nv12_16", "nv12_32"):
+        Hi, Wi, Ho, Wo = prm["H_IN"], prm["W_IN"], prm["H_OUT"], prm["W_OUT"]
+        img = rng.integers(0, 256, size=(Hi * 3 // 2, Wi), dtype=np.uint8)
+        img[0, :4] = (0, 255, 0, 255)  # the extremes of both planes
+        img[Hi, :4] = (0, 255, 255, 0)
+        ti = torch.from_numpy(img).to(dev)
+        f16 = kind == "nv12_16"
+        to = torch.full((1, 3, Ho, Wo), float("nan"), dtype=torch.float16 if f16 else torch.float32, device=dev)
+        fn = R.wwref_nv12_decode_f16 if f16 else R.wwref_nv12_decode_f32
+        rc = fn(ti.data_ptr(), to.data_ptr(), Hi, Wi, Ho, Wo, stream)
+        torch.cuda.synchronize()
+        assert rc == 0, f"{name}: reference launcher returned {rc}"
+        out.update(nv12=img, out=to.cpu().numpy(), H_IN=Hi, W_IN=Wi, H_OUT=Ho, W_OUT=Wo)
     else:
         raise ValueError(kind)
     return out
@@ -103,8 +123,11 @@ def run_case(name: str, kind: str, prm: dict) -> dict:
 
 def main() -> None:
     out_dir = sys.argv[1] if len(sys.argv) > 1 else HERE
+    only = sys.argv[2] if len(sys.argv) > 2 else ""
     os.makedirs(out_dir, exist_ok=True)
     for name, kind, prm in CASES:
+        if only not in name:
+            continue
         d = run_case(name, kind, prm)
         np.savez(os.path.join(out_dir, f"{name}.npz"), **d)
         print(f"{name}: {kind} {prm} -> out {d['out'].shape} {d['out'].dtype}")

@@ -29,6 +29,14 @@ def test_oracle_reproduces_reference(orc, name):
     elif kind == "stem3":
         got = orc.stem_ref3(g["vol"], g["w0"], g["b0"], g["w1"], g["b1"], g["w2"], g["b2"])
         assert np.array_equal(got.view(np.uint16), g["out"].view(np.uint16))
+    elif kind in ("nv12_16", "nv12_32"):
+        f16 = kind == "nv12_16"
+        got = orc.nv12_decode(g["nv12"], int(g["H_OUT"]), int(g["W_OUT"]), out_f16=f16)
+        assert got.shape == g["out"].shape
+        if f16:
+            assert np.array_equal(got.view(np.uint16), g["out"].view(np.uint16))
+        else:
+            assert np.array_equal(got.view(np.uint32), g["out"].view(np.uint32))
     else:
         pytest.fail(f"unknown fixture kind {kind}")
 

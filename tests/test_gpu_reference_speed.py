@@ -1,0 +1,127 @@
+"""The reference's own CUDA kernels, rebuilt for sm_100a (oracle/_ref), timed
+beside this library's kernels on the same B200 and the same inputs: the
+baseline the reference would give on this hardware.
+
+* Group-wise correlation: the reference has no grouped kernel, so its
+  composition is one launchCorrVolume<__half> per (b, g) (B = 1, C = C/G).
+  Compared with ww_corr_volume (one launch, bit-identical output) and with
+  the fused ww_corr_cost_stem3d, which also runs the G -> Cout stem the
+  reference has no kernel for.
+* The reference CostStem3D at its native shape [1, 1, 48, 32, 40] against
+  ww_cost_stem3d_ref3 (bit-identical output).
+
+CUDA events, 10 warm-up calls, median of 50 timed calls (each call timed on
+its own).  The table is printed (pytest -s) and, when WW_REF_SPEED_OUT names
+a file, written there as JSON.  The assertions only check the outputs and that
+the library is not slower than the reference composition."""
+import json
+import os
+import statistics
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+def _median_us(torch, fn, warmup=10, reps=50):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(ts)
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    import oracle
+    import whirlwind_trt_plugins_b200 as ww
+    ref = oracle.ref_lib()
+    return torch, ww, ref
+
+
+RESULTS = {}
+
+
+def _save():
+    out = os.environ.get("WW_REF_SPEED_OUT")
+    if out:
+        with open(out, "w") as f:
+            json.dump(RESULTS, f, indent=1)
+
+
+@pytest.mark.parametrize("cfg_id", [2, 3, 5, 4])
+def test_grouped_correlation_vs_reference_kernels(env, cfg_id):
+    torch, ww, ref = env
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs_torch
+    cfg = CONFIGS[cfg_id]
+    x = make_inputs_torch(cfg, torch.device("cuda", 0))
+    L, R = x["left"], x["right"]
+    B, C, H, W = L.shape
+    D, G = cfg.D, cfg.G
+    vol_ref = torch.empty((B, G, D, H, W), dtype=torch.float16, device="cuda")
+    vol = torch.empty_like(vol_ref)
+    out = torch.empty((B, cfg.Cout, D, H, W), dtype=torch.float16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run_ref():
+        assert ref.wwref_corr_volume_grouped_f16(L.data_ptr(), R.data_ptr(), vol_ref.data_ptr(), B, C, H, W, D, G,
+                                                 s) == 0
+
+    def run_ours():
+        ww.corr_volume(L, R, D, G, out=vol)
+
+    def run_fused():
+        ww.corr_cost_stem3d(L, R, x["w"], x["b"], D, G, act=cfg.act, out=out)
+
+    t_ref = _median_us(torch, run_ref, reps=10 if cfg_id == 4 else 50)
+    t_ours = _median_us(torch, run_ours, reps=10 if cfg_id == 4 else 50)
+    t_fused = _median_us(torch, run_fused, reps=10 if cfg_id == 4 else 50)
+    torch.cuda.synchronize()
+    assert torch.equal(vol, vol_ref)
+    vox = B * D * H * W
+    RESULTS[f"corr_c{cfg_id}"] = {
+        "reference_per_bg_us": t_ref, "ww_corr_volume_us": t_ours, "ww_corr_cost_stem3d_us": t_fused,
+        "reference_launches": B * G, "voxels": vox,
+        "reference_vox_per_s": vox / (t_ref * 1e-6), "fused_vox_per_s": vox / (t_fused * 1e-6)}
+    print(f"\nconfig {cfg_id}: reference CorrVolume x{B * G} launches {t_ref:9.1f} us | "
+          f"ww_corr_volume {t_ours:8.1f} us | fused corr+stem {t_fused:8.1f} us")
+    _save()
+    assert t_ours < t_ref
+
+
+def test_native_stem_vs_reference_kernel(env):
+    torch, ww, ref = env
+    g = torch.Generator(device="cuda").manual_seed(7)
+    vol = torch.randn((1, 1, 48, 32, 40), generator=g, device="cuda").half()
+    ws = [(torch.randn((n,), generator=g, device="cuda") * s).half()
+          for n, s in ((108, 0.2), (4, 0.1), (432, 0.2), (4, 0.1), (108, 0.2), (1, 0.1))]
+    o_ref = torch.empty_like(vol)
+    o = torch.empty_like(vol)
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run_ref():
+        assert ref.wwref_cost_stem3d(vol.data_ptr(), o_ref.data_ptr(), *[w.data_ptr() for w in ws], 1, 48, 32, 40,
+                                     s) == 0
+
+    def run_ours():
+        ww.cost_stem3d_ref3(vol, *ws, out=o)
+
+    t_ref = _median_us(torch, run_ref)
+    t_ours = _median_us(torch, run_ours)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref)
+    RESULTS["stem3_native"] = {"reference_us": t_ref, "ww_cost_stem3d_ref3_us": t_ours}
+    print(f"\nnative CostStem3D [1,1,48,32,40]: reference {t_ref:.2f} us | ww_cost_stem3d_ref3 {t_ours:.2f} us")
+    _save()
+    assert t_ours < 2 * t_ref

@@ -16,6 +16,8 @@ reference project):
 * ``cost_stem3d(vol, w, b, act)``                      -- generalised 3-input stem
 * ``corr_cost_stem3d(left, right, w, b, max_disp, num_groups, act)`` -- fused op
 * ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
+* ``nv12_decode(nv12, out_h, out_w, dtype)``           -- Nv12Decode
+  (``src/plugins/nv12_decode/nv12_decode_kernel.hpp:20-28``)
 
 The plugin-level classes mirroring the reference's IPluginV3 plugins live in
 ``whirlwind_trt_plugins_b200.plugins``; row-band sharding over several GPUs in
@@ -28,7 +30,7 @@ import os
 
 __all__ = [
     "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "cost_stem3d",
-    "corr_cost_stem3d", "corr_cost_stem3d_band", "fold_bn", "device_error", "clear_device_error",
+    "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "fold_bn", "device_error", "clear_device_error",
     "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF",
 ]
 
@@ -67,6 +69,7 @@ def _load() -> ctypes.CDLL:
     L.ww_cost_stem3d.argtypes = [p, p, p, p] + [i] * 7 + [p]
     L.ww_corr_cost_stem3d.argtypes = [p, p, p, p, p] + [i] * 8 + [p]
     L.ww_corr_cost_stem3d_band.argtypes = [p, p, p, p, p] + [i] * 12 + [p]
+    L.ww_nv12_decode.argtypes = [p, p] + [i] * 6 + [p]
     L.ww_fold_bn_f16.argtypes = [p, p, p, i, i, p, p]
     L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.ww_clear_device_error.argtypes = []
@@ -214,6 +217,34 @@ def corr_cost_stem3d_band(left_band, right_band, w, b, max_disp: int, num_groups
         left_band.data_ptr(), right_band.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
         B, C, num_groups, H, W, max_disp, Cout, act, in_row0, in_rows, out_row0, out_rows,
         _stream_ptr(stream)))
+    return out
+
+
+def nv12_decode(nv12, out_h: int = 224, out_w: int = 288, dtype=None, out=None, stream=None):
+    """NV12 [B, H_IN * 3 / 2, W_IN] (uint8 or int8 bytes, or one [H*3/2, W]
+    image) -> planar RGB [B, 3, out_h, out_w] in [-1, 1], fp16 (default) or
+    fp32: bilinear resize (align_corners = False, clamped), full-range
+    BT.601.  Every batch item is decoded."""
+    torch = _torch()
+    if not isinstance(nv12, torch.Tensor) or not nv12.is_cuda:
+        raise TypeError("nv12 must be a CUDA tensor")
+    if nv12.dtype not in (torch.uint8, torch.int8):
+        raise TypeError("nv12 must hold uint8 (or int8) bytes")
+    if not nv12.is_contiguous():
+        raise ValueError("nv12 must be contiguous")
+    x = nv12 if nv12.dim() == 3 else nv12.unsqueeze(0)
+    if x.dim() != 3 or x.shape[1] % 3 != 0:
+        raise ValueError("nv12 must be [B, H_IN * 3 / 2, W_IN]")
+    B, H_NV12, W_IN = x.shape
+    dtype = dtype or torch.float16
+    dt = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}.get(dtype)
+    if dt is None:
+        raise TypeError("output dtype must be float16 or float32")
+    if out is None:
+        out = torch.empty((B, 3, out_h, out_w), dtype=dtype, device=x.device)
+    _dev(out, "out", dtype)
+    _check("ww_nv12_decode", _lib.ww_nv12_decode(x.data_ptr(), out.data_ptr(), dt, B, H_NV12 * 2 // 3, W_IN,
+                                                 out_h, out_w, _stream_ptr(stream)))
     return out
 
 

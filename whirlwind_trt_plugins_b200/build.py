@@ -33,6 +33,7 @@ SOURCES = [
     "cost_stem3d_ref3.cu",
     "stem_tc.cu",
     "tensor_map.cu",
+    "nv12_decode.cu",
     "plugin_core.cpp",
 ]
 TRT_SOURCES = ["trt/ww_trt_plugins.cpp"]

@@ -15,6 +15,8 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                    const void* b, void* out, int B, int C, int G, int H, int W, int D, int Cout,
                    int act, int in_row0, int in_rows, int out_row0, int out_rows,
                    cudaStream_t stream) noexcept;
+int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT,
+                       int W_OUT, cudaStream_t stream) noexcept;
 
 namespace {
 
@@ -128,6 +130,13 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
     if (left == nullptr || right == nullptr) return WW_ERR_NULL_POINTER;
     return ww::stem_tc_launch(nullptr, left, right, w, b, out, B, C, G, H, W, D, Cout, act, in_row0,
                               in_rows, out_row0, out_rows, static_cast<cudaStream_t>(stream));
+}
+
+int ww_nv12_decode(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT, int W_OUT,
+                   void* stream)
+{
+    return ww::nv12_decode_launch(nv12, out, dtype, B, H_IN, W_IN, H_OUT, W_OUT,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 int ww_fold_bn_f16(const float* w, const float* scale, const float* bias, int cout, int k,

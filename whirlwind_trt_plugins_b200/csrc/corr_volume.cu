@@ -2,8 +2,8 @@
 //
 //   out[b, g, d, h, w] = scale( sum_{c in group g} L[b,c,h,w] * R[b,c,h,w-d] ),  +0 if w-d < 0
 //
-// Semantics follow the reference kernels exactly (corr_volume_kernel.cu:80-117
-// naive, :146-268 fast): an fp32 fma chain over the group's channels in
+// Semantics follow the reference kernels exactly (corr_volume_kernel.cu:52-88
+// naive, :118-239 fast): an fp32 fma chain over the group's channels in
 // channel order starting from +0, then either acc / C (what the naive kernel
 // does) or acc * (1/C) (what the fast kernel does), rounded to the output
 // type.  Which of the two the reference would have used for the equivalent
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
 
 // Scale rule of the reference kernel that launchCorrVolume<T> would run for a
 // call with (B, C, H, W, D): 1 = naive kernel (acc / C), 0 = fast kernel
-// (acc * 1/C).  Restates corr_volume_kernel.cu:280-354 (pickTileW and
+// (acc * 1/C).  Restates corr_volume_kernel.cu:251-326 (pickTileW and
 // fastPathApplies) for the current device's SM count.
 int corr_scale_div(bool is_half, int B, int C, int H, int W, int D, int sm_count) noexcept
 {

@@ -9,13 +9,18 @@
 // the reference kernel whatever the tiling, so the tiling is B200's own:
 //
 //   * one CTA = a 4 x 8 x 8 (D, H, W) output brick of one batch item, 256
-//     threads, one output per thread in the last stage;
+//     threads;
 //   * the input brick (+3 halo) and both intermediate bricks live in shared
 //     memory as fp32 copies of fp16 values (no conversion in the inner loops),
 //     36 KB, so six CTAs fit an SM;
-//   * weights and biases are staged once per CTA into shared memory as fp32.
-// The native shape [1, 1, 48, 32, 40] is launch-bound (~60K outputs): the
-// grid is 240 CTAs, all resident in one wave on 148 SMs.
+//   * weights and biases are staged once per CTA into shared memory as fp32;
+//   * each thread computes a run of NX consecutive outputs of one channel
+//     (conv_run): NX independent fma chains advance together, one row segment
+//     of NX + 2 inputs is loaded per (ci, kd, kh) and reused by the three kw
+//     taps.  Each chain still runs in (ci, kd, kh, kw) order.
+// The native shape [1, 1, 48, 32, 40] is latency-bound (~60K outputs, 240
+// CTAs in one wave on 148 SMs): the independent chains are what hides the
+// fma and shared-memory latency.
 
 #include "ww_common.cuh"
 
@@ -37,6 +42,34 @@ __device__ __forceinline__ float relu6(float v) { return fminf(6.0f, fmaxf(0.0f,
 __device__ __forceinline__ bool inside(int d, int h, int w, int D, int H, int W)
 {
     return d >= 0 && d < D && h >= 0 && h < H && w >= 0 && w < W;
+}
+
+// NX consecutive outputs (x0 .. x0 + NX - 1, row y, plane z of the output
+// brick) of one output channel of a 3x3x3 convolution over CIN channels of a
+// shared-memory brick (channel stride cs, plane SH x SW).  w: [CIN][27].
+template <int CIN, int NX>
+__device__ __forceinline__ void conv_run(const float* src, int cs, int SH, int SW, int z, int y, int x0,
+                                         const float* w, float (&acc)[NX])
+{
+#pragma unroll
+    for (int j = 0; j < NX; ++j) acc[j] = 0.0f;
+#pragma unroll
+    for (int ci = 0; ci < CIN; ++ci)
+#pragma unroll
+        for (int kd = 0; kd < 3; ++kd)
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh) {
+                const float* row = src + ci * cs + ((z + kd) * SH + y + kh) * SW + x0;
+                float seg[NX + 2];
+#pragma unroll
+                for (int t = 0; t < NX + 2; ++t) seg[t] = row[t];
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    const float wv = w[ci * 27 + kd * 9 + kh * 3 + kw];
+#pragma unroll
+                    for (int j = 0; j < NX; ++j) acc[j] = __fmaf_rn(seg[j + kw], wv, acc[j]);
+                }
+            }
 }
 
 __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
@@ -83,63 +116,59 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
     }
     __syncthreads();
 
-    // Stage 0: 1 -> 4 over the stage-0 brick, origin (od0-2, oh0-2, ow0-2).
-    for (int i = tid; i < 4 * A_VOL; i += kThreads) {
-        const int co = i / A_VOL, r0 = i - co * A_VOL;
-        const int z = r0 / (A_H * A_W), r = r0 - z * A_H * A_W, y = r / A_W, x = r - y * A_W;
-        float acc = 0.0f;
-#pragma unroll
-        for (int kd = 0; kd < 3; ++kd)
-#pragma unroll
-            for (int kh = 0; kh < 3; ++kh)
-#pragma unroll
-                for (int kw = 0; kw < 3; ++kw)
-                    acc = __fmaf_rn(s_in[((z + kd) * I_H + y + kh) * I_W + x + kw], sw0[co * 27 + kd * 9 + kh * 3 + kw], acc);
-        acc = __fadd_rn(acc, sb0[co]);
-        const bool in_vol = inside(od0 - 2 + z, oh0 - 2 + y, ow0 - 2 + x, D, H, W);
-        s_a[i] = in_vol ? __half2float(__float2half_rn(relu6(acc))) : 0.0f;
-    }
-    __syncthreads();
-
-    // Stage 1: 4 -> 4 over the stage-1 brick, origin (od0-1, oh0-1, ow0-1).
-    for (int i = tid; i < 4 * B_VOL; i += kThreads) {
-        const int co = i / B_VOL, r0 = i - co * B_VOL;
-        const int z = r0 / (B_H * B_W), r = r0 - z * B_H * B_W, y = r / B_W, x = r - y * B_W;
-        float acc = 0.0f;
-#pragma unroll
-        for (int ci = 0; ci < 4; ++ci)
-#pragma unroll
-            for (int kd = 0; kd < 3; ++kd)
-#pragma unroll
-                for (int kh = 0; kh < 3; ++kh)
-#pragma unroll
-                    for (int kw = 0; kw < 3; ++kw)
-                        acc = __fmaf_rn(s_a[ci * A_VOL + ((z + kd) * A_H + y + kh) * A_W + x + kw],
-                                        sw1[(co * 4 + ci) * 27 + kd * 9 + kh * 3 + kw], acc);
-        acc = __fadd_rn(acc, sb1[co]);
-        const bool in_vol = inside(od0 - 1 + z, oh0 - 1 + y, ow0 - 1 + x, D, H, W);
-        s_b[i] = in_vol ? __half2float(__float2half_rn(relu6(acc))) : 0.0f;
-    }
-    __syncthreads();
-
-    // Stage 2: 4 -> 1, one output per thread.
+    // Stage 0: 1 -> 4 over the stage-0 brick, origin (od0-2, oh0-2, ow0-2);
+    // runs of 4 along the 12-wide rows.
     {
-        const int z = tid / (TH * TW), r = tid - z * TH * TW, y = r / TW, x = r - y * TW;
-        const int gd = od0 + z, gh = oh0 + y, gw = ow0 + x;
-        if (gd < D && gh < H && gw < W) {
-            float acc = 0.0f;
+        constexpr int NX = 4, NG = A_W / NX;
+        for (int i = tid; i < 4 * A_D * A_H * NG; i += kThreads) {
+            const int co = i / (A_D * A_H * NG), r0 = i - co * (A_D * A_H * NG);
+            const int z = r0 / (A_H * NG), r = r0 - z * (A_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
+            float acc[NX];
+            conv_run<1, NX>(s_in, 0, I_H, I_W, z, y, x0, sw0 + co * 27, acc);
 #pragma unroll
-            for (int ci = 0; ci < 4; ++ci)
+            for (int j = 0; j < NX; ++j) {
+                const float v = __fadd_rn(acc[j], sb0[co]);
+                const bool in_vol = inside(od0 - 2 + z, oh0 - 2 + y, ow0 - 2 + x0 + j, D, H, W);
+                s_a[co * A_VOL + (z * A_H + y) * A_W + x0 + j] = in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+
+    // Stage 1: 4 -> 4 over the stage-1 brick, origin (od0-1, oh0-1, ow0-1);
+    // runs of 5 along the 10-wide rows.
+    {
+        constexpr int NX = 5, NG = B_W / NX;
+        for (int i = tid; i < 4 * B_D * B_H * NG; i += kThreads) {
+            const int co = i / (B_D * B_H * NG), r0 = i - co * (B_D * B_H * NG);
+            const int z = r0 / (B_H * NG), r = r0 - z * (B_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
+            float acc[NX];
+            conv_run<4, NX>(s_a, A_VOL, A_H, A_W, z, y, x0, sw1 + co * 108, acc);
 #pragma unroll
-                for (int kd = 0; kd < 3; ++kd)
+            for (int j = 0; j < NX; ++j) {
+                const float v = __fadd_rn(acc[j], sb1[co]);
+                const bool in_vol = inside(od0 - 1 + z, oh0 - 1 + y, ow0 - 1 + x0 + j, D, H, W);
+                s_b[co * B_VOL + (z * B_H + y) * B_W + x0 + j] = in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+
+    // Stage 2: 4 -> 1, runs of 2 along the 8-wide output rows.
+    {
+        constexpr int NX = 2, NG = TW / NX;
+        if (tid < TD * TH * NG) {
+            const int z = tid / (TH * NG), r = tid - z * (TH * NG), y = r / NG, x0 = (r - y * NG) * NX;
+            float acc[NX];
+            conv_run<4, NX>(s_b, B_VOL, B_H, B_W, z, y, x0, sw2, acc);
+            const int gd = od0 + z, gh = oh0 + y;
 #pragma unroll
-                    for (int kh = 0; kh < 3; ++kh)
-#pragma unroll
-                        for (int kw = 0; kw < 3; ++kw)
-                            acc = __fmaf_rn(s_b[ci * B_VOL + ((z + kd) * B_H + y + kh) * B_W + x + kw],
-                                            sw2[ci * 27 + kd * 9 + kh * 3 + kw], acc);
-            acc = __fadd_rn(acc, sb2[0]);
-            out[i64(b) * vol + (i64(gd) * H + gh) * W + gw] = __float2half_rn(relu6(acc));
+            for (int j = 0; j < NX; ++j) {
+                const int gw = ow0 + x0 + j;
+                if (gd < D && gh < H && gw < W)
+                    out[i64(b) * vol + (i64(gd) * H + gh) * W + gw] =
+                        __float2half_rn(relu6(__fadd_rn(acc[j], sb2[0])));
+            }
         }
     }
 }

@@ -203,4 +203,64 @@ int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act, co
     return st == WW_SUCCESS ? 0 : 1;
 }
 
+// ------------------------------------------------------------- Nv12Decode
+
+// nv12_decode.cpp:26-39: the output is declared fp32 whatever the input
+// (TensorRT picks fp16 or fp32 through supportsFormatCombination).
+int ww_plugin_nv12_decode_output_dtype(int nb_inputs, int32_t* out_dtype)
+{
+    (void)nb_inputs;
+    if (out_dtype == nullptr) return 1;
+    *out_dtype = WW_DTYPE_FLOAT;
+    return 0;
+}
+
+// nv12_decode.cpp:41-60: [B, H_IN * 3 / 2, W_IN] -> [B, 3, out_h, out_w].
+int ww_plugin_nv12_decode_output_dims(int out_h, int out_w, int nb_inputs, const ww_tensor_desc_t* inputs,
+                                      ww_tensor_desc_t* out)
+{
+    if (nb_inputs != 1 || inputs == nullptr || out == nullptr) return 1;
+    *out = inputs[0];
+    out->nb_dims = 4;
+    out->dims[0] = inputs[0].dims[0];
+    out->dims[1] = 3;
+    out->dims[2] = out_h;
+    out->dims[3] = out_w;
+    out->dtype = WW_DTYPE_FLOAT;
+    return 0;
+}
+
+// nv12_decode.cpp:62-86: LINEAR; position 0 INT8 only (the bytes are uint8
+// NV12 values; accepting fp32 would let TensorRT insert a sign-extending
+// cast), the output fp16 or fp32.
+int ww_plugin_nv12_decode_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs, int nb_outputs)
+{
+    if (in_out == nullptr || nb_inputs != 1 || nb_outputs != 1) return 0;
+    if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
+    const ww_tensor_desc_t& d = in_out[pos];
+    if (d.format != WW_FORMAT_LINEAR) return 0;
+    if (pos == 0) return d.dtype == WW_DTYPE_INT8;
+    return d.dtype == WW_DTYPE_HALF || d.dtype == WW_DTYPE_FLOAT;
+}
+
+// nv12_decode.cpp:88-115: rank-3 input, H_IN = 2 d[1] / 3, W_IN = d[2]; the
+// output dtype selects the kernel; 0 or 1.  Every batch item is decoded (the
+// reference launches batch 0 only).
+int ww_plugin_nv12_decode_enqueue(int out_h, int out_w, const ww_tensor_desc_t* in_desc,
+                                  const ww_tensor_desc_t* out_desc, const void* const* inputs,
+                                  void* const* outputs, void* stream)
+{
+    if (in_desc == nullptr || out_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    const ww_tensor_desc_t& d = in_desc[0];
+    if (d.nb_dims != 3) return 1;
+    for (int i = 0; i < 3; ++i)
+        if (!fits_int(d.dims[i])) return 1;
+    const int dt = out_desc[0].dtype;
+    if (dt != WW_DTYPE_HALF && dt != WW_DTYPE_FLOAT) return 1;
+    const int H_IN = static_cast<int>(d.dims[1] * 2 / 3);
+    const int st = ww_nv12_decode(inputs[0], outputs[0], dt, static_cast<int>(d.dims[0]), H_IN,
+                                  static_cast<int>(d.dims[2]), out_h, out_w, stream);
+    return st == WW_SUCCESS ? 0 : 1;
+}
+
 }  // extern "C"

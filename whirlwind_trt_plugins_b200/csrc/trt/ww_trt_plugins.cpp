@@ -6,13 +6,15 @@
 //       -lww_trt_plugins -L<tensorrt>/lib -lnvinfer -o libww_trt_shim.so
 //
 // It registers the creators the reference registers
-// (src/register_plugins.cpp:15-16) under the same names and version --
-// "CorrVolume" v"1" with field max_disp (default 48), "CostStem3D" v"1" with
-// no required field -- plus the fused "CorrCostStem3D" v"1".  Every method is
+// (src/register_plugins.cpp:15-18, the stereo path and the camera decode)
+// under the same names and version -- "CorrVolume" v"1" with field max_disp
+// (default 48), "CostStem3D" v"1" with no required field, "Nv12Decode" v"1"
+// with fields out_h / out_w (224 / 288) -- plus the fused "CorrCostStem3D".  Every method is
 // a thin forwarder to the ww_plugin_* functions of the C ABI (plugin_core.cpp),
 // which carry the logic of the reference's IPluginV3 methods
 // (src/plugins/corr_volume/corr_volume.cpp:23-139,
-// src/plugins/cost_stem_3d/cost_stem_3d.cpp:14-97).  One plugin class serves
+// src/plugins/cost_stem_3d/cost_stem_3d.cpp:14-97,
+// src/plugins/nv12_decode/nv12_decode.cpp:16-146).  One plugin class serves
 // all three ops; the op kind selects the forwarding target.
 #include <NvInferRuntime.h>
 #include <NvInferRuntimePlugin.h>
@@ -30,13 +32,15 @@ namespace ww_trt {
 
 using namespace nvinfer1;
 
-enum class Op { kCorrVolume, kCostStem3D, kCorrCostStem3D };
+enum class Op { kCorrVolume, kCostStem3D, kCorrCostStem3D, kNv12Decode };
 
 // Integer fields an op carries; every op stores all three, serialises its own.
 struct Fields {
     int32_t max_disp = 48;
     int32_t num_groups = 1;
     int32_t act = WW_ACT_RELU;
+    int32_t out_h = 224;
+    int32_t out_w = 288;
 };
 
 constexpr char const* kVersion = "1";
@@ -47,6 +51,7 @@ char const* op_name(Op op) noexcept
         case Op::kCorrVolume: return "CorrVolume";
         case Op::kCostStem3D: return "CostStem3D";
         case Op::kCorrCostStem3D: return "CorrCostStem3D";
+        case Op::kNv12Decode: return "Nv12Decode";
     }
     return "";
 }
@@ -58,6 +63,7 @@ std::vector<char const*> op_fields(Op op)
         case Op::kCorrVolume: return {"max_disp", "num_groups"};
         case Op::kCostStem3D: return {"act"};
         case Op::kCorrCostStem3D: return {"max_disp", "num_groups", "act"};
+        case Op::kNv12Decode: return {"out_h", "out_w"};
     }
     return {};
 }
@@ -67,6 +73,8 @@ int32_t* field_slot(Fields& f, char const* name) noexcept
     if (std::strcmp(name, "max_disp") == 0) return &f.max_disp;
     if (std::strcmp(name, "num_groups") == 0) return &f.num_groups;
     if (std::strcmp(name, "act") == 0) return &f.act;
+    if (std::strcmp(name, "out_h") == 0) return &f.out_h;
+    if (std::strcmp(name, "out_w") == 0) return &f.out_w;
     return nullptr;
 }
 
@@ -122,7 +130,9 @@ public:
                                int32_t nbInputs) const noexcept override
     {
         if (nbOutputs < 1 || nbInputs < 1) return 1;
-        out[0] = in[0];
+        // Nv12Decode declares fp32 and lets the format choice pick fp16 or
+        // fp32 (nv12_decode.cpp:26-39); the others follow input 0.
+        out[0] = mOp == Op::kNv12Decode ? DataType::kFLOAT : in[0];
         return 0;
     }
 
@@ -157,6 +167,14 @@ public:
                 out[0] = in[0];
                 out[0].d[1] = in[1].d[0];
                 return 0;
+            case Op::kNv12Decode:  // [B, H * 3 / 2, W] -> [B, 3, out_h, out_w]
+                if (nbInputs != 1 || in[0].nbDims != 3) return 1;
+                out[0].nbDims = 4;
+                out[0].d[0] = in[0].d[0];
+                out[0].d[1] = eb.constant(3);
+                out[0].d[2] = eb.constant(mFields.out_h);
+                out[0].d[3] = eb.constant(mFields.out_w);
+                return 0;
             case Op::kCorrCostStem3D:  // [B, Cout, D, H, W]
                 if (nbInputs != 4 || in[0].nbDims != 4 || in[2].nbDims != 5) return 1;
                 out[0].nbDims = 5;
@@ -184,6 +202,8 @@ public:
                 return ww_plugin_cost_stem3d_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
             case Op::kCorrCostStem3D:
                 return ww_plugin_corr_cost_stem3d_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
+            case Op::kNv12Decode:
+                return ww_plugin_nv12_decode_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
         }
         return false;
     }
@@ -202,7 +222,7 @@ public:
         return 0;
     }
 
-    int32_t enqueue(PluginTensorDesc const* inDesc, PluginTensorDesc const*, void const* const* inputs,
+    int32_t enqueue(PluginTensorDesc const* inDesc, PluginTensorDesc const* outDesc, void const* const* inputs,
                     void* const* outputs, void*, cudaStream_t stream) noexcept override
     {
         // Descriptors of the inputs: 2 (CorrVolume), 7 or 3 (CostStem3D), 4 (fused).
@@ -219,6 +239,12 @@ public:
             case Op::kCorrCostStem3D:
                 return ww_plugin_corr_cost_stem3d_enqueue(mFields.max_disp, mFields.num_groups, mFields.act,
                                                           d.data(), inputs, outputs, stream);
+            case Op::kNv12Decode: {
+                if (outDesc == nullptr) return 1;
+                const ww_tensor_desc_t od = to_ww(outDesc[0]);
+                return ww_plugin_nv12_decode_enqueue(mFields.out_h, mFields.out_w, d.data(), &od, inputs, outputs,
+                                                     stream);
+            }
         }
         return 1;
     }
@@ -302,6 +328,9 @@ struct CostStem3DCreator final : WwCreator {
 struct CorrCostStem3DCreator final : WwCreator {
     CorrCostStem3DCreator() : WwCreator(Op::kCorrCostStem3D) {}
 };
+struct Nv12DecodeCreator final : WwCreator {
+    Nv12DecodeCreator() : WwCreator(Op::kNv12Decode) {}
+};
 
 }  // namespace ww_trt
 
@@ -310,7 +339,9 @@ struct CorrCostStem3DCreator final : WwCreator {
 using ww_trt::CorrCostStem3DCreator;
 using ww_trt::CorrVolumeCreator;
 using ww_trt::CostStem3DCreator;
+using ww_trt::Nv12DecodeCreator;
 
 REGISTER_TENSORRT_PLUGIN(CorrVolumeCreator);
 REGISTER_TENSORRT_PLUGIN(CostStem3DCreator);
 REGISTER_TENSORRT_PLUGIN(CorrCostStem3DCreator);
+REGISTER_TENSORRT_PLUGIN(Nv12DecodeCreator);

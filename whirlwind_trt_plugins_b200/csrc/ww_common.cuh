@@ -28,7 +28,7 @@ inline int launch_status(const char* where) noexcept
 
 // Streaming-multiprocessor count and opt-in shared memory of the current
 // device, cached per device ordinal.  (The reference caches per host thread,
-// corr_volume_kernel.cu:55-69, which returns the wrong count when one thread
+// corr_volume_kernel.cu:26-40, which returns the wrong count when one thread
 // drives several devices.)
 struct DeviceInfo {
     int sm_count = 0;

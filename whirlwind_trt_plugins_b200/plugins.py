@@ -20,9 +20,11 @@ Reference plugins (paths relative to the reference project):
   form (vol, w, b) with field ``act``.
 * ``CorrCostStem3D`` v1 (extension, the fused op): fields ``max_disp``,
   ``num_groups``, ``act``.
+* ``Nv12Decode`` v1, fields ``out_h`` (224), ``out_w`` (288) --
+  ``src/plugins/nv12_decode/nv12_decode.cpp:16-146``.
 
 Descriptors are :class:`TensorDesc` (dims, dtype, format); dtypes use
-TensorRT's numbering (0 = kFLOAT, 1 = kHALF), format 0 = kLINEAR.
+TensorRT's numbering (0 = kFLOAT, 1 = kHALF, 2 = kINT8), format 0 = kLINEAR.
 """
 from __future__ import annotations
 
@@ -31,11 +33,12 @@ from dataclasses import dataclass, field
 
 from . import lib
 
-__all__ = ["TensorDesc", "CorrVolumePlugin", "CostStem3DPlugin", "CorrCostStem3DPlugin",
+__all__ = ["TensorDesc", "CorrVolumePlugin", "CostStem3DPlugin", "CorrCostStem3DPlugin", "Nv12DecodePlugin",
            "PluginCreator", "get_plugin_creator", "registered_creators"]
 
 DTYPE_FLOAT = 0
 DTYPE_HALF = 1
+DTYPE_INT8 = 2
 FORMAT_LINEAR = 0
 
 
@@ -68,7 +71,8 @@ class TensorDesc:
     def of(t) -> "TensorDesc":
         """Descriptor of a torch tensor (fp16 or fp32)."""
         import torch
-        dt = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}.get(t.dtype, -1)
+        dt = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT, torch.int8: DTYPE_INT8,
+              torch.uint8: DTYPE_INT8}.get(t.dtype, -1)
         return TensorDesc(tuple(t.shape), dt, FORMAT_LINEAR)
 
 
@@ -213,6 +217,41 @@ class CorrCostStem3DPlugin(_PluginBase):
                                                         ctypes.c_void_p(_stream(stream)))
 
 
+class Nv12DecodePlugin(_PluginBase):
+    """``Nv12Decode`` (nv12_decode.cpp:16-127): one INT8 input (uint8 NV12
+    bytes), one fp16/fp32 output; decodes every batch item."""
+    NAME = "Nv12Decode"
+
+    def __init__(self, out_h: int = 224, out_w: int = 288):
+        super().__init__()
+        self.out_h = int(out_h)
+        self.out_w = int(out_w)
+
+    def get_fields_to_serialize(self) -> dict:
+        return {"out_h": self.out_h, "out_w": self.out_w}
+
+    def get_output_data_types(self, input_types) -> list:
+        out = ctypes.c_int32(-1)
+        if lib().ww_plugin_nv12_decode_output_dtype(len(input_types), ctypes.byref(out)) != 0:
+            raise ValueError("getOutputDataTypes failed")
+        return [out.value]
+
+    def get_output_shapes(self, inputs) -> list:
+        out = _Desc()
+        if lib().ww_plugin_nv12_decode_output_dims(self.out_h, self.out_w, len(inputs), _descs(inputs),
+                                                   ctypes.byref(out)) != 0:
+            raise ValueError("Nv12Decode takes one [B, H * 3 / 2, W] input")
+        return [TensorDesc._from_c(out).dims]
+
+    def supports_format_combination(self, pos: int, in_out, nb_inputs: int, nb_outputs: int) -> bool:
+        return bool(lib().ww_plugin_nv12_decode_supports_format(pos, _descs(in_out), nb_inputs, nb_outputs))
+
+    def enqueue(self, input_desc, output_desc, inputs, outputs, stream=None) -> int:
+        return lib().ww_plugin_nv12_decode_enqueue(self.out_h, self.out_w, _descs(input_desc),
+                                                   _descs(output_desc), _ptrs(inputs), _ptrs(outputs),
+                                                   ctypes.c_void_p(_stream(stream)))
+
+
 @dataclass
 class PluginCreator:
     """IPluginCreatorV3One counterpart: name, version, field names, create."""
@@ -244,6 +283,7 @@ _CREATORS = {
     ("CorrVolume", "1"): PluginCreator(CorrVolumePlugin, {"max_disp": 48, "num_groups": 1}),
     ("CostStem3D", "1"): PluginCreator(CostStem3DPlugin, {"act": 0}),
     ("CorrCostStem3D", "1"): PluginCreator(CorrCostStem3DPlugin, {"max_disp": 48, "num_groups": 1, "act": 0}),
+    ("Nv12Decode", "1"): PluginCreator(Nv12DecodePlugin, {"out_h": 224, "out_w": 288}),
 }
 
 

@@ -26,6 +26,9 @@ Printed (rank 0, one JSON line):
              on a bounded row band of the same workload, all host threads.
 --impl reference times that CPU implementation on the same workload
 (rank 0 only; the other ranks exit 0).
+
+--op nv12_decode measures the camera decode instead (one GPU, NV12_B 720p
+frames -> 224 x 288 fp16; HBM roofline; the C oracle as the CPU baseline).
 """
 from __future__ import annotations
 
@@ -62,6 +65,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode"], default="corr_cost_stem3d",
+                    help="corr_cost_stem3d (the headline) or nv12_decode (the camera decode, one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
@@ -195,8 +200,122 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+# Nv12Decode workload: a batch of 720p NV12 camera frames decoded and
+# resized to the plugin's default 224 x 288 output, fp16.
+NV12_B, NV12_H, NV12_W, NV12_OH, NV12_OW = 8, 720, 1280, 224, 288
+
+
+def bench_nv12(args):
+    """One step = ww_nv12_decode over NV12_B frames (one GPU).  value: output
+    pixels/s; roofline against HBM with bytes = the whole NV12 input + the
+    fp16 output (the downscale reads fewer input bytes than that)."""
+    import numpy as np
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    torch.cuda.set_device(0)
+    B, H, W, OH, OW = NV12_B, NV12_H, NV12_W, NV12_OH, NV12_OW
+    in_bytes, out_bytes = B * H * 3 // 2 * W, B * 3 * OH * OW * 2
+    n_sets = max(2, -(-160 * 2**20 // (in_bytes + out_bytes)))  # > 126 MB of L2
+    g = torch.Generator(device="cuda").manual_seed(1)
+    sets = [(torch.randint(0, 256, (B, H * 3 // 2, W), generator=g, device="cuda", dtype=torch.uint8),
+             torch.empty((B, 3, OH, OW), dtype=torch.float16, device="cuda")) for _ in range(n_sets)]
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        x, o = sets[i % n_sets]
+        ww.nv12_decode(x, OH, OW, out=o, stream=stream)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        print(f"profile run: nv12_decode, {max(3, args.warmup)} + {args.steps} launches", flush=True)
+        return
+    with ClockSampler(0) as clk:
+        t_end = time.time() + 1.0
+        i = 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    px = B * OH * OW
+    value = px / (ms * 1e-3)
+    # end to end from pinned host frames, three streams
+    hosts = [torch.empty((B, H * 3 // 2, W), dtype=torch.uint8, pin_memory=True) for _ in range(3)]
+    for h in hosts:
+        h.copy_(sets[0][0])
+    houts = [torch.empty((B, 3, OH, OW), dtype=torch.float16, pin_memory=True) for _ in range(3)]
+    dins = [torch.empty_like(sets[0][0]) for _ in range(3)]
+    douts = [torch.empty_like(sets[0][1]) for _ in range(3)]
+    strs = [torch.cuda.Stream() for _ in range(3)]
+
+    def e2e_step(i):
+        k = i % 3
+        with torch.cuda.stream(strs[k]):
+            dins[k].copy_(hosts[k], non_blocking=True)
+            ww.nv12_decode(dins[k], OH, OW, out=douts[k], stream=strs[k])
+            houts[k].copy_(douts[k], non_blocking=True)
+
+    for i in range(6):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for st in strs:
+        st.wait_stream(stream)
+    n_e2e = max(3, min(args.steps, 60))
+    for i in range(n_e2e):
+        e2e_step(i)
+    for st in strs:
+        stream.wait_stream(st)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e = {"value": px * n_e2e / (f0.elapsed_time(f1) * 1e-3), "unit": "pixels/s",
+           "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": n_e2e, "streams": 3}
+    peaks = load_peaks()
+    gbs = (in_bytes + out_bytes) / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        n = oracle.nthreads_default()
+        img = sets[0][0][:2].cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 5.0:
+            oracle.nv12_decode(img, OH, OW, nthreads=n)
+            reps += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": 2 * OH * OW * reps / dt, "unit": "pixels/s", "cores": n, "kind": "port",
+               "sample": f"{reps} decodes of 2 frames in the C oracle, {dt:.1f} s"}
+    line = {
+        "metric": "nv12 decode output pixels/s", "value": value, "unit": "pixels/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8->f16", "data": "synthetic (uniform random bytes)",
+        "config": {"workload": f"nv12_decode: B={B} {H}x{W} NV12 -> 3x{OH}x{OW} fp16",
+                   "l2": f"{n_sets} rotating input/output sets > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["src"]},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.op == "nv12_decode":
+        if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
+            bench_nv12(args)
+        return
     from whirlwind_trt_plugins_b200.configs import CONFIGS
     cfg = CONFIGS[args.config]
     if cfg.Cout == 0:

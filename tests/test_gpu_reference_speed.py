@@ -9,6 +9,9 @@ baseline the reference would give on this hardware.
   reference has no kernel for.
 * The reference CostStem3D at its native shape [1, 1, 48, 32, 40] against
   ww_cost_stem3d_ref3 (bit-identical output).
+* The reference Nv12Decode (one launch per frame, as its launcher takes one
+  image) on 8 720p frames -> 224 x 288 fp16 against one ww_nv12_decode call
+  (bit-identical output).
 
 CUDA events, 10 warm-up calls, median of 50 timed calls (each call timed on
 its own).  The table is printed (pytest -s) and, when WW_REF_SPEED_OUT names
@@ -125,3 +128,31 @@ def test_native_stem_vs_reference_kernel(env):
     print(f"\nnative CostStem3D [1,1,48,32,40]: reference {t_ref:.2f} us | ww_cost_stem3d_ref3 {t_ours:.2f} us")
     _save()
     assert t_ours < 2 * t_ref
+
+
+def test_nv12_decode_vs_reference_kernel(env):
+    torch, ww, ref = env
+    B, H, W, OH, OW = 8, 720, 1280, 224, 288
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randint(0, 256, (B, H * 3 // 2, W), generator=g, device="cuda", dtype=torch.uint8)
+    o_ref = torch.empty((B, 3, OH, OW), dtype=torch.float16, device="cuda")
+    o = torch.empty_like(o_ref)
+    s = torch.cuda.current_stream().cuda_stream
+    frame_in, frame_out = H * 3 // 2 * W, 3 * OH * OW * 2
+
+    def run_ref():
+        for b in range(B):
+            assert ref.wwref_nv12_decode_f16(x.data_ptr() + b * frame_in, o_ref.data_ptr() + b * frame_out, H, W,
+                                             OH, OW, s) == 0
+
+    def run_ours():
+        ww.nv12_decode(x, OH, OW, out=o)
+
+    t_ref = _median_us(torch, run_ref)
+    t_ours = _median_us(torch, run_ours)
+    torch.cuda.synchronize()
+    assert torch.equal(o.view(torch.int16), o_ref.view(torch.int16))
+    RESULTS["nv12_b8_720p"] = {"reference_us": t_ref, "reference_launches": B, "ww_nv12_decode_us": t_ours}
+    print(f"\nNv12Decode 8 x 720p -> 224x288: reference x{B} launches {t_ref:.2f} us | ww_nv12_decode {t_ours:.2f} us")
+    _save()
+    assert t_ours < t_ref

@@ -70,6 +70,7 @@
 #include "ww_common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace ww {
 
@@ -998,6 +999,28 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     if (warp == kMmaWarp) tmem_dealloc(tmem_base, p.tmem_cols);
 }
 
+// Raise a kernel's dynamic shared-memory limit to the device's opt-in maximum
+// once per (kernel, device) instead of on every launch: the attribute is a
+// driver call, and launches with any smaller size then need nothing.
+bool ensure_smem_limit(const void* kernel, int device, int optin) noexcept
+{
+    constexpr int kSlots = 64;
+    static std::mutex mu;
+    static const void* done_fn[kSlots];
+    static int done_dev[kSlots];
+    static int n_done = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n_done; ++i)
+        if (done_fn[i] == kernel && done_dev[i] == device) return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) return false;
+    if (n_done < kSlots) {
+        done_fn[n_done] = kernel;
+        done_dev[n_done] = device;
+        ++n_done;
+    }
+    return true;
+}
+
 uint32_t pow2_cols(uint32_t c)
 {
     uint32_t r = 32;
@@ -1156,10 +1179,11 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     const long long grid = col_tiles * p.n_strips;
     if (grid > 0x7fffffffLL) return WW_ERR_UNSUPPORTED;
 
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return WW_ERR_DEVICE;
     auto launch = [&](auto kernel) -> int {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-            cudaSuccess)
-            return launch_status("ww_cost_stem3d");
+        if (!ensure_smem_limit(reinterpret_cast<const void*>(kernel), device, dev.smem_optin))
+            return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
         kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
         return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
     };

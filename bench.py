@@ -65,8 +65,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode"], default="corr_cost_stem3d",
-                    help="corr_cost_stem3d (the headline) or nv12_decode (the camera decode, one GPU)")
+    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode", "disparity_regression"],
+                    default="corr_cost_stem3d",
+                    help="corr_cost_stem3d (the headline), nv12_decode (the camera decode, one GPU) or "
+                         "disparity_regression (soft-argmin after aggregation, one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
@@ -310,11 +312,120 @@ def bench_nv12(args):
     print(json.dumps(line), flush=True)
 
 
+# Disparity regression workload: the aggregated cost of the batched config
+# (config 4: B = 64, D = 48, 94 x 312), fp16 in and out, soft-argmin.
+DISP_B, DISP_D, DISP_H, DISP_W = 64, 48, 94, 312
+
+
+def bench_disparity(args):
+    """One step = ww_disparity_regression over a [DISP_B, DISP_D, DISP_H,
+    DISP_W] fp16 cost (180 MB, larger than L2; two rotating sets).  value:
+    output pixels/s; roofline against HBM with bytes = the cost read once +
+    the fp16 disparity written."""
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    torch.cuda.set_device(0)
+    B, D, H, W = DISP_B, DISP_D, DISP_H, DISP_W
+    in_bytes, out_bytes = B * D * H * W * 2, B * H * W * 2
+    n_sets = 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    sets = [((torch.randn((B, D, H, W), generator=g, device="cuda") * 2.0).half(),
+             torch.empty((B, 1, H, W), dtype=torch.float16, device="cuda")) for _ in range(n_sets)]
+    stream = torch.cuda.current_stream()
+    mode = ww.DISP_SOFTARGMIN
+
+    def step(i):
+        x, o = sets[i % n_sets]
+        ww.disparity_regression(x, mode, out=o, stream=stream)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        print(f"profile run: disparity_regression, {max(3, args.warmup)} + {args.steps} launches", flush=True)
+        return
+    with ClockSampler(0) as clk:
+        t_end = time.time() + 1.0
+        i = 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    px = B * H * W
+    value = px / (ms * 1e-3)
+    e2e = None
+    if not args.no_e2e:
+        # end to end from pinned host memory: the cost up, the disparity back
+        host = torch.empty((B, D, H, W), dtype=torch.float16, pin_memory=True)
+        host.copy_(sets[0][0])
+        hout = torch.empty((B, 1, H, W), dtype=torch.float16, pin_memory=True)
+        din, dout = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1])
+
+        def e2e_step():
+            din.copy_(host, non_blocking=True)
+            ww.disparity_regression(din, mode, out=dout, stream=stream)
+            hout.copy_(dout, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        n_e2e = max(3, min(args.steps, 20))
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e = {"value": px * n_e2e / (f0.elapsed_time(f1) * 1e-3), "unit": "pixels/s",
+               "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": n_e2e}
+    peaks = load_peaks()
+    gbs = (in_bytes + out_bytes) / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        n = oracle.nthreads_default()
+        sample = sets[0][0][:2].cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 5.0:
+            oracle.disparity_regression(sample, mode, out_f16=True, nthreads=n)
+            reps += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": 2 * H * W * reps / dt, "unit": "pixels/s", "cores": n, "kind": "port",
+               "sample": f"{reps} regressions of 2 of the {B} cost volumes in the C oracle, {dt:.1f} s"}
+    line = {
+        "metric": "disparity regression output pixels/s", "value": value, "unit": "pixels/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16->f32 math->f16",
+        "data": "synthetic (cost ~ 2 N(0,1))",
+        "config": {"workload": f"disparity_regression soft-argmin: cost [{B}, {D}, {H}, {W}] fp16 -> [{B}, 1, {H}, {W}]",
+                   "l2": f"{n_sets} rotating sets of {in_bytes / 1e6:.0f} MB > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["src"]},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.op == "nv12_decode":
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
             bench_nv12(args)
+        return
+    if args.op == "disparity_regression":
+        if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
+            bench_disparity(args)
         return
     from whirlwind_trt_plugins_b200.configs import CONFIGS
     cfg = CONFIGS[args.config]

@@ -63,6 +63,10 @@ typedef enum ww_dtype { WW_DTYPE_FLOAT = 0, WW_DTYPE_HALF = 1, WW_DTYPE_INT8 = 2
 /* Activation of the generalised / fused stem. */
 typedef enum ww_act { WW_ACT_RELU = 0, WW_ACT_RELU6 = 1 } ww_act_t;
 
+/* Disparity regression: softmax over the disparities of +cost (similarity)
+ * or -cost (matching cost). */
+typedef enum ww_disp_mode { WW_DISP_SOFTARGMAX = 0, WW_DISP_SOFTARGMIN = 1 } ww_disp_mode_t;
+
 /* Tensor format, same value as nvinfer1::TensorFormat::kLINEAR. */
 #define WW_FORMAT_LINEAR 0
 
@@ -147,6 +151,21 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
 int ww_nv12_decode(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT, int W_OUT,
                    void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Disparity regression (soft-argmax / soft-argmin), the step after the 3-D
+ * aggregation of a stereo network.  The reference library has no such op;
+ * the formula below is its specification:
+ *   disp[b, 0, h, w] = sum_d d * softmax_d(s * cost[b, d, h, w]),
+ *   s = +1 (WW_DISP_SOFTARGMAX) or -1 (WW_DISP_SOFTARGMIN).
+ * cost : [B, D, H, W] (= [B, 1, D, H, W]), in_dtype WW_DTYPE_HALF or
+ *        WW_DTYPE_FLOAT, finite values; D >= 1
+ * out  : [B, 1, H, W], out_dtype WW_DTYPE_HALF or WW_DTYPE_FLOAT
+ * fp32 arithmetic: within 1e-5 relative (of max(|disp|, 1)) of the exact
+ * value; an fp16 output is that value rounded to nearest.
+ * ------------------------------------------------------------------------- */
+int ww_disparity_regression(const void* cost, void* out, int in_dtype, int out_dtype, int B, int D, int H, int W,
+                            int mode, void* stream);
+
 /* BatchNorm folding on the host: w16[o, :] = fp16(w[o, :] * scale[o]) computed in
  * fp32, b16[o] = fp16(bias[o]); k = Cin * 27.  Host memory only. */
 int ww_fold_bn_f16(const float* w, const float* scale, const float* bias, int cout, int k,
@@ -217,6 +236,18 @@ int ww_plugin_nv12_decode_supports_format(int pos, const ww_tensor_desc_t* in_ou
 int ww_plugin_nv12_decode_enqueue(int out_h, int out_w, const ww_tensor_desc_t* in_desc,
                                   const ww_tensor_desc_t* out_desc, const void* const* inputs,
                                   void* const* outputs, void* stream);
+
+/* "DisparityRegression" v"1" (extension; no reference counterpart): field
+ * mode (0 soft-argmax, 1 soft-argmin; default 0); input cost [B, D, H, W] or
+ * [B, 1, D, H, W] fp16 or fp32; output [B, 1, H, W], same dtype as the
+ * input. */
+int ww_plugin_disparity_regression_output_dims(int nb_inputs, const ww_tensor_desc_t* inputs,
+                                               ww_tensor_desc_t* out);
+int ww_plugin_disparity_regression_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                                   int nb_outputs);
+int ww_plugin_disparity_regression_enqueue(int mode, const ww_tensor_desc_t* in_desc,
+                                           const ww_tensor_desc_t* out_desc, const void* const* inputs,
+                                           void* const* outputs, void* stream);
 
 /* Device error word written by bounded waits inside the tensor-core kernels
  * (0 = none).  Reading it synchronises the current device.  Clearing resets

@@ -71,6 +71,7 @@ def lib() -> ctypes.CDLL:
         L.orc_f32_to_f16_array.restype = None
         L.orc_hw_threads.restype = i
         L.orc_nv12_decode.argtypes = [p] + [i] * 6 + [p, i]
+        L.orc_disparity_regression.argtypes = [p] + [i] * 7 + [p, i]
         _lib = L
     return _lib
 
@@ -234,4 +235,24 @@ def nv12_decode(nv12: np.ndarray, H_OUT: int, W_OUT: int, out_f16: bool = True, 
     out = np.empty((B, 3, H_OUT, W_OUT), dtype=np.uint16 if out_f16 else np.float32)
     _check(lib().orc_nv12_decode(_ptr(a), B, H_IN, W_IN, H_OUT, W_OUT, int(out_f16), _ptr(out), nthreads),
            "nv12_decode")
+    return out.view(np.float16) if out_f16 else out
+
+
+def disparity_regression(cost: np.ndarray, mode: int = 0, out_f16: bool = False, nthreads: int = 0) -> np.ndarray:
+    """cost [B, D, H, W] (or [B, 1, D, H, W]) fp16/fp32 -> disparity [B, 1, H, W]:
+    sum_d d * softmax_d(s * cost), s = +1 (mode 0) or -1 (mode 1), in double,
+    rounded once to fp32 (or fp16).  No reference counterpart exists; the
+    formula is the specification."""
+    a = np.ascontiguousarray(cost)
+    if a.ndim == 5:
+        assert a.shape[1] == 1
+        a = a[:, 0]
+    if a.dtype == np.float16:
+        in_f16, a = 1, a.view(np.uint16)
+    else:
+        in_f16, a = 0, np.ascontiguousarray(a, dtype=np.float32)
+    B, D, H, W = a.shape
+    out = np.empty((B, 1, H, W), dtype=np.uint16 if out_f16 else np.float32)
+    _check(lib().orc_disparity_regression(_ptr(a), in_f16, B, D, H, W, mode, int(out_f16), _ptr(out), nthreads),
+           "disparity_regression")
     return out.view(np.float16) if out_f16 else out

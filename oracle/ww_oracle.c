@@ -17,6 +17,9 @@
  *     then + bias, ReLU6, fp16 RNE; positions outside the volume are zero
  *     for the next stage (cost_stem_3d_kernel.cu:115-232).
  *
+ *   - disparity regression has no reference counterpart: it is evaluated
+ *     from its formula in double (no parity pin exists for it).
+ *
  * Skipping a zero-padding tap is bit-identical to multiplying the staged
  * zero the reference multiplies: the accumulator starts at +0 and an RNE
  * fma chain never produces -0 from a +0 start, so acc + (+-0) == acc.
@@ -611,5 +614,66 @@ int orc_nv12_decode(const uint8_t* nv12, int B, int H_IN, int W_IN, int H_OUT, i
     c.suv_h = (float)(H_IN >> 1) / (float)H_OUT;
     c.suv_w = (float)(W_IN >> 1) / (float)W_OUT;
     orc_parallel_for((int64_t)B * H_OUT, nthreads, nv12_body, &c);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* Disparity regression (no reference counterpart; the formula is the  */
+/* specification): disp = sum_d d * softmax_d(s * cost), in double.    */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    const void* cost;
+    int in_f16, out_f16;
+    int D, H, W;
+    double sign;
+    void* out;
+} disp_ctx;
+
+static void disp_body(void* vctx, int64_t row)
+{
+    const disp_ctx* c = (const disp_ctx*)vctx;
+    const int64_t plane = (int64_t)c->H * c->W;
+    const int64_t b = row / c->H, h = row % c->H;
+    for (int w = 0; w < c->W; ++w) {
+        const int64_t base = b * c->D * plane + h * c->W + w;
+        double m = -INFINITY;
+        for (int d = 0; d < c->D; ++d) {
+            const int64_t i = base + (int64_t)d * plane;
+            const double x = c->sign * (c->in_f16 ? (double)orc_f16_to_f32(((const uint16_t*)c->cost)[i])
+                                                  : (double)((const float*)c->cost)[i]);
+            if (x > m) m = x;
+        }
+        double s = 0.0, t = 0.0;
+        for (int d = 0; d < c->D; ++d) {
+            const int64_t i = base + (int64_t)d * plane;
+            const double x = c->sign * (c->in_f16 ? (double)orc_f16_to_f32(((const uint16_t*)c->cost)[i])
+                                                  : (double)((const float*)c->cost)[i]);
+            const double e = exp(x - m);
+            s += e;
+            t += (double)d * e;
+        }
+        const double disp = t / s;
+        const int64_t o = b * plane + h * c->W + w;
+        if (c->out_f16) ((uint16_t*)c->out)[o] = half_from_double(disp);
+        else ((float*)c->out)[o] = (float)disp;
+    }
+}
+
+int orc_disparity_regression(const void* cost, int in_f16, int B, int D, int H, int W, int mode, int out_f16,
+                             void* out, int nthreads)
+{
+    if (cost == NULL || out == NULL) return 1;
+    if (B < 0 || D < 1 || H < 0 || W < 0 || (mode != 0 && mode != 1)) return 2;
+    disp_ctx c;
+    c.cost = cost;
+    c.in_f16 = in_f16;
+    c.out_f16 = out_f16;
+    c.D = D;
+    c.H = H;
+    c.W = W;
+    c.sign = mode == 1 ? -1.0 : 1.0;
+    c.out = out;
+    orc_parallel_for((int64_t)B * H, nthreads, disp_body, &c);
     return 0;
 }

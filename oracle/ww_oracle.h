@@ -112,6 +112,15 @@ int orc_hw_threads(void);
 int orc_nv12_decode(const uint8_t* nv12, int B, int H_IN, int W_IN, int H_OUT, int W_OUT, int out_f16,
                     void* out, int nthreads);
 
+/* Disparity regression, the step after the 3-D aggregation (no reference
+ * counterpart; this formula is its specification):
+ *   disp[b, h, w] = sum_d d * softmax_d(s * cost[b, d, h, w]),
+ * s = +1 (mode 0, soft-argmax) or -1 (mode 1, soft-argmin); cost [B, D, H, W]
+ * fp16 bit patterns if in_f16, else fp32; evaluated in double and rounded
+ * once to the output type (fp16 bit patterns if out_f16, else fp32).     */
+int orc_disparity_regression(const void* cost, int in_f16, int B, int D, int H, int W, int mode, int out_f16,
+                             void* out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ def test_front_end_captures_and_replays():
     g = torch.Generator(device="cuda").manual_seed(2)
     frames = torch.randint(0, 256, (2, 96 * 3 // 2, 128), generator=g, device="cuda", dtype=torch.uint8)
     vol1 = torch.randn((1, 1, 16, 12, 20), generator=g, device="cuda").half()
+    agg = torch.randn((2, 24, 10, 16), generator=g, device="cuda").half()
     ws = [(torch.randn((n,), generator=g, device="cuda") * 0.2).half() for n in (108, 4, 432, 4, 108, 1)]
 
     outs = {
@@ -25,6 +26,7 @@ def test_front_end_captures_and_replays():
         "corr": torch.empty((B, cfg.G, cfg.D, H, W), dtype=torch.float16, device="cuda"),
         "nv12": torch.empty((2, 3, 60, 80), dtype=torch.float16, device="cuda"),
         "stem3": torch.empty_like(vol1),
+        "disp": torch.empty((2, 1, 10, 16), dtype=torch.float16, device="cuda"),
     }
 
     def run():
@@ -32,6 +34,7 @@ def test_front_end_captures_and_replays():
         ww.corr_volume(L, R, cfg.D, cfg.G, out=outs["corr"])
         ww.nv12_decode(frames, 60, 80, out=outs["nv12"])
         ww.cost_stem3d_ref3(vol1, *ws, out=outs["stem3"])
+        ww.disparity_regression(agg, ww.DISP_SOFTARGMIN, out=outs["disp"])
 
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())

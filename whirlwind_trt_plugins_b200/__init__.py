@@ -18,6 +18,8 @@ reference project):
 * ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
 * ``nv12_decode(nv12, out_h, out_w, dtype)``           -- Nv12Decode
   (``src/plugins/nv12_decode/nv12_decode_kernel.hpp:20-28``)
+* ``disparity_regression(cost, mode, dtype)``          -- soft-argmax / soft-argmin
+  after the 3-D aggregation (no reference counterpart; specified by its formula)
 
 The plugin-level classes mirroring the reference's IPluginV3 plugins live in
 ``whirlwind_trt_plugins_b200.plugins``; row-band sharding over several GPUs in
@@ -30,8 +32,8 @@ import os
 
 __all__ = [
     "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "cost_stem3d",
-    "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "fold_bn", "device_error", "clear_device_error",
-    "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF",
+    "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "disparity_regression", "fold_bn", "device_error",
+    "clear_device_error", "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF", "DISP_SOFTARGMAX", "DISP_SOFTARGMIN",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libww_trt_plugins.so")
@@ -40,6 +42,8 @@ DTYPE_FLOAT = 0
 DTYPE_HALF = 1
 ACT_RELU = 0
 ACT_RELU6 = 1
+DISP_SOFTARGMAX = 0
+DISP_SOFTARGMIN = 1
 
 STATUS = {
     0: "success", 1: "CUDA launch or runtime call failed", 2: "invalid tensor shape",
@@ -70,6 +74,7 @@ def _load() -> ctypes.CDLL:
     L.ww_corr_cost_stem3d.argtypes = [p, p, p, p, p] + [i] * 8 + [p]
     L.ww_corr_cost_stem3d_band.argtypes = [p, p, p, p, p] + [i] * 12 + [p]
     L.ww_nv12_decode.argtypes = [p, p] + [i] * 6 + [p]
+    L.ww_disparity_regression.argtypes = [p, p] + [i] * 7 + [p]
     L.ww_fold_bn_f16.argtypes = [p, p, p, i, i, p, p]
     L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.ww_clear_device_error.argtypes = []
@@ -245,6 +250,38 @@ def nv12_decode(nv12, out_h: int = 224, out_w: int = 288, dtype=None, out=None, 
     _dev(out, "out", dtype)
     _check("ww_nv12_decode", _lib.ww_nv12_decode(x.data_ptr(), out.data_ptr(), dt, B, H_NV12 * 2 // 3, W_IN,
                                                  out_h, out_w, _stream_ptr(stream)))
+    return out
+
+
+def disparity_regression(cost, mode: int = DISP_SOFTARGMAX, dtype=None, out=None, stream=None):
+    """cost [B, D, H, W] or [B, 1, D, H, W] (fp16 or fp32) -> disparity
+    [B, 1, H, W] = sum_d d * softmax_d(s * cost), s = +1 (DISP_SOFTARGMAX,
+    cost is a similarity) or -1 (DISP_SOFTARGMIN, cost is a matching cost);
+    fp32 arithmetic, output dtype = input dtype unless `dtype` is given."""
+    torch = _torch()
+    if not isinstance(cost, torch.Tensor) or not cost.is_cuda:
+        raise TypeError("cost must be a CUDA tensor")
+    dts = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}
+    if cost.dtype not in dts:
+        raise TypeError("cost must be float16 or float32")
+    if not cost.is_contiguous():
+        raise ValueError("cost must be contiguous")
+    if cost.dim() == 5 and cost.shape[1] == 1:
+        B, _, D, H, W = cost.shape
+    elif cost.dim() == 4:
+        B, D, H, W = cost.shape
+    else:
+        raise ValueError("cost must be [B, D, H, W] or [B, 1, D, H, W]")
+    if mode not in (DISP_SOFTARGMAX, DISP_SOFTARGMIN):
+        raise ValueError("mode must be DISP_SOFTARGMAX or DISP_SOFTARGMIN")
+    dtype = dtype or cost.dtype
+    if dtype not in dts:
+        raise TypeError("output dtype must be float16 or float32")
+    if out is None:
+        out = torch.empty((B, 1, H, W), dtype=dtype, device=cost.device)
+    _dev(out, "out", dtype)
+    _check("ww_disparity_regression", _lib.ww_disparity_regression(
+        cost.data_ptr(), out.data_ptr(), dts[cost.dtype], dts[dtype], B, D, H, W, mode, _stream_ptr(stream)))
     return out
 
 

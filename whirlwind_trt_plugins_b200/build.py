@@ -34,6 +34,7 @@ SOURCES = [
     "stem_tc.cu",
     "tensor_map.cu",
     "nv12_decode.cu",
+    "disparity_regression.cu",
     "plugin_core.cpp",
 ]
 TRT_SOURCES = ["trt/ww_trt_plugins.cpp"]

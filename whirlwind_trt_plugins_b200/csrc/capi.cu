@@ -17,6 +17,8 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                    cudaStream_t stream) noexcept;
 int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT,
                        int W_OUT, cudaStream_t stream) noexcept;
+int disparity_regression_launch(const void* cost, void* out, int in_dtype, int out_dtype, int B, int D, int H,
+                                int W, int mode, cudaStream_t stream) noexcept;
 
 namespace {
 
@@ -137,6 +139,13 @@ int ww_nv12_decode(const void* nv12, void* out, int dtype, int B, int H_IN, int 
 {
     return ww::nv12_decode_launch(nv12, out, dtype, B, H_IN, W_IN, H_OUT, W_OUT,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int ww_disparity_regression(const void* cost, void* out, int in_dtype, int out_dtype, int B, int D, int H, int W,
+                            int mode, void* stream)
+{
+    return ww::disparity_regression_launch(cost, out, in_dtype, out_dtype, B, D, H, W, mode,
+                                           static_cast<cudaStream_t>(stream));
 }
 
 int ww_fold_bn_f16(const float* w, const float* scale, const float* bias, int cout, int k,

@@ -13,14 +13,22 @@
 //   * the input brick (+3 halo) and both intermediate bricks live in shared
 //     memory as fp32 copies of fp16 values (no conversion in the inner loops),
 //     36 KB, so six CTAs fit an SM;
-//   * weights and biases are staged once per CTA into shared memory as fp32;
-//   * each thread computes a run of NX consecutive outputs of one channel
-//     (conv_run): NX independent fma chains advance together, one row segment
-//     of NX + 2 inputs is loaded per (ci, kd, kh) and reused by the three kw
-//     taps.  Each chain still runs in (ci, kd, kh, kw) order.
+//   * weights and biases are staged once per CTA into shared memory as fp32,
+//     the 4-output stages' weights as one float4 (the 4 output channels) per
+//     (input channel, tap);
+//   * in the two 4-output stages each thread computes a run of NX
+//     consecutive positions for all 4 output channels (conv_run_x4): one row
+//     segment of NX + 2 inputs is loaded per (ci, kd, kh) and reused by the
+//     three kw taps and the four output channels, so a row costs NX + 2
+//     scalar loads and 3 broadcast float4 loads for 12 NX fmas; the last
+//     stage (one output channel) blocks 2 rows x 2 columns per thread;
+//   * every global load of the staging phase is issued before the first
+//     shared-memory store, so the brick costs one memory latency, not eight.
+// Shared-memory bandwidth, not the fma rate, bounded the first version of
+// this kernel (one output channel per thread, one weight load per tap).
 // The native shape [1, 1, 48, 32, 40] is latency-bound (~60K outputs, 240
-// CTAs in one wave on 148 SMs): the independent chains are what hides the
-// fma and shared-memory latency.
+// CTAs in one wave on 148 SMs): the 4 NX independent chains per thread are
+// what hides the fma and shared-memory latency.
 
 #include "ww_common.cuh"
 
@@ -44,15 +52,19 @@ __device__ __forceinline__ bool inside(int d, int h, int w, int D, int H, int W)
     return d >= 0 && d < D && h >= 0 && h < H && w >= 0 && w < W;
 }
 
-// NX consecutive outputs (x0 .. x0 + NX - 1, row y, plane z of the output
-// brick) of one output channel of a 3x3x3 convolution over CIN channels of a
-// shared-memory brick (channel stride cs, plane SH x SW).  w: [CIN][27].
+// NX consecutive positions (x0 .. x0 + NX - 1, row y, plane z of the
+// destination brick) of all 4 output channels of a 3x3x3 convolution over CIN
+// channels of a shared-memory brick (channel stride cs, plane SH x SW).
+// wq: [CIN][27] float4, one lane per output channel.  Each acc[co][j] is an
+// fp32 fma chain in (ci, kd, kh, kw) order starting from +0.
 template <int CIN, int NX>
-__device__ __forceinline__ void conv_run(const float* src, int cs, int SH, int SW, int z, int y, int x0,
-                                         const float* w, float (&acc)[NX])
+__device__ __forceinline__ void conv_run_x4(const float* src, int cs, int SH, int SW, int z, int y, int x0,
+                                            const float4* wq, float (&acc)[4][NX])
 {
 #pragma unroll
-    for (int j = 0; j < NX; ++j) acc[j] = 0.0f;
+    for (int co = 0; co < 4; ++co)
+#pragma unroll
+        for (int j = 0; j < NX; ++j) acc[co][j] = 0.0f;
 #pragma unroll
     for (int ci = 0; ci < CIN; ++ci)
 #pragma unroll
@@ -65,9 +77,14 @@ __device__ __forceinline__ void conv_run(const float* src, int cs, int SH, int S
                 for (int t = 0; t < NX + 2; ++t) seg[t] = row[t];
 #pragma unroll
                 for (int kw = 0; kw < 3; ++kw) {
-                    const float wv = w[ci * 27 + kd * 9 + kh * 3 + kw];
+                    const float4 wv = wq[ci * 27 + kd * 9 + kh * 3 + kw];
 #pragma unroll
-                    for (int j = 0; j < NX; ++j) acc[j] = __fmaf_rn(seg[j + kw], wv, acc[j]);
+                    for (int j = 0; j < NX; ++j) {
+                        acc[0][j] = __fmaf_rn(seg[j + kw], wv.x, acc[0][j]);
+                        acc[1][j] = __fmaf_rn(seg[j + kw], wv.y, acc[1][j]);
+                        acc[2][j] = __fmaf_rn(seg[j + kw], wv.z, acc[2][j]);
+                        acc[3][j] = __fmaf_rn(seg[j + kw], wv.w, acc[3][j]);
+                    }
                 }
             }
 }
@@ -82,13 +99,15 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
     __shared__ float s_in[I_VOL];
     __shared__ float s_a[4 * A_VOL];
     __shared__ float s_b[4 * B_VOL];
-    __shared__ float s_w[kWeights];
-    float* sw0 = s_w;
-    float* sb0 = sw0 + 108;
-    float* sw1 = sb0 + 4;
-    float* sb1 = sw1 + 432;
-    float* sw2 = sb1 + 4;
-    float* sb2 = sw2 + 108;
+    __shared__ float4 s_w0q[27];       // [tap] -> 4 output channels
+    __shared__ float4 s_w1q[4 * 27];   // [ci][tap] -> 4 output channels
+    __shared__ float s_w2[108];        // [ci][tap]
+    __shared__ float s_bias[9];        // b0[4], b1[4], b2
+    float* sw0q = reinterpret_cast<float*>(s_w0q);
+    float* sw1q = reinterpret_cast<float*>(s_w1q);
+    const float* sb0 = s_bias;
+    const float* sb1 = s_bias + 4;
+    const float* sb2 = s_bias + 8;
 
     const int tid = threadIdx.x;
     const int b = blockIdx.z / n_dtiles;
@@ -98,77 +117,147 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
     const int64_t vol = i64(D) * H * W;
     const __half* src = in + i64(b) * vol;
 
-    for (int i = tid; i < kWeights; i += kThreads) {
-        float v;
-        if (i < 108) v = __half2float(w0[i]);
-        else if (i < 112) v = __half2float(b0[i - 108]);
-        else if (i < 544) v = __half2float(w1[i - 112]);
-        else if (i < 548) v = __half2float(b1[i - 544]);
-        else if (i < 656) v = __half2float(w2[i - 548]);
-        else v = __half2float(b2[0]);
-        s_w[i] = v;
+    // w0 [co][27] -> s_w0q[tap].co; w1 [co][ci][27] -> s_w1q[ci * 27 + tap].co.
+    // All of a thread's global loads are issued before its first shared store.
+    {
+        constexpr int kIt = (kWeights + kThreads - 1) / kThreads;
+        __half v[kIt];
+#pragma unroll
+        for (int k = 0; k < kIt; ++k) {
+            const int i = tid + k * kThreads;
+            const __half* src_w = i < 108 ? w0 + i : i < 112 ? b0 + (i - 108) : i < 544 ? w1 + (i - 112)
+                                : i < 548 ? b1 + (i - 544) : i < 656 ? w2 + (i - 548) : b2;
+            v[k] = i < kWeights ? *src_w : __float2half_rn(0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < kIt; ++k) {
+            const int i = tid + k * kThreads;
+            const float f = __half2float(v[k]);
+            if (i < 108) {
+                const int co = i / 27, tap = i - co * 27;
+                sw0q[tap * 4 + co] = f;
+            } else if (i < 112) {
+                s_bias[i - 108] = f;
+            } else if (i < 544) {
+                const int r = i - 112, co = r / 108, q = r - co * 108;  // q = ci * 27 + tap
+                sw1q[q * 4 + co] = f;
+            } else if (i < 548) {
+                s_bias[4 + i - 544] = f;
+            } else if (i < 656) {
+                s_w2[i - 548] = f;
+            } else if (i < kWeights) {
+                s_bias[8] = f;
+            }
+        }
     }
     // Input brick, origin (od0-3, oh0-3, ow0-3), zero outside the volume.
-    for (int i = tid; i < I_VOL; i += kThreads) {
-        const int z = i / (I_H * I_W), r = i - z * I_H * I_W, y = r / I_W, x = r - y * I_W;
-        const int gd = od0 - 3 + z, gh = oh0 - 3 + y, gw = ow0 - 3 + x;
-        s_in[i] = inside(gd, gh, gw, D, H, W) ? __half2float(src[(i64(gd) * H + gh) * W + gw]) : 0.0f;
+    {
+        constexpr int kIt = (I_VOL + kThreads - 1) / kThreads;
+        __half v[kIt];
+#pragma unroll
+        for (int k = 0; k < kIt; ++k) {
+            const int i = tid + k * kThreads;
+            const int z = i / (I_H * I_W), r = i - z * I_H * I_W, y = r / I_W, x = r - y * I_W;
+            const int gd = od0 - 3 + z, gh = oh0 - 3 + y, gw = ow0 - 3 + x;
+            v[k] = (i < I_VOL && inside(gd, gh, gw, D, H, W)) ? src[(i64(gd) * H + gh) * W + gw]
+                                                               : __float2half_rn(0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < kIt; ++k) {
+            const int i = tid + k * kThreads;
+            if (i < I_VOL) s_in[i] = __half2float(v[k]);
+        }
     }
     __syncthreads();
 
     // Stage 0: 1 -> 4 over the stage-0 brick, origin (od0-2, oh0-2, ow0-2);
-    // runs of 4 along the 12-wide rows.
+    // runs of 6 along the 12-wide rows, all 4 channels per thread (192 runs).
     {
-        constexpr int NX = 4, NG = A_W / NX;
-        for (int i = tid; i < 4 * A_D * A_H * NG; i += kThreads) {
-            const int co = i / (A_D * A_H * NG), r0 = i - co * (A_D * A_H * NG);
-            const int z = r0 / (A_H * NG), r = r0 - z * (A_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
-            float acc[NX];
-            conv_run<1, NX>(s_in, 0, I_H, I_W, z, y, x0, sw0 + co * 27, acc);
+        constexpr int NX = 6, NG = A_W / NX;
+        for (int i = tid; i < A_D * A_H * NG; i += kThreads) {
+            const int z = i / (A_H * NG), r = i - z * (A_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
+            float acc[4][NX];
+            conv_run_x4<1, NX>(s_in, 0, I_H, I_W, z, y, x0, s_w0q, acc);
 #pragma unroll
             for (int j = 0; j < NX; ++j) {
-                const float v = __fadd_rn(acc[j], sb0[co]);
                 const bool in_vol = inside(od0 - 2 + z, oh0 - 2 + y, ow0 - 2 + x0 + j, D, H, W);
-                s_a[co * A_VOL + (z * A_H + y) * A_W + x0 + j] = in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+#pragma unroll
+                for (int co = 0; co < 4; ++co) {
+                    const float v = __fadd_rn(acc[co][j], sb0[co]);
+                    s_a[co * A_VOL + (z * A_H + y) * A_W + x0 + j] =
+                        in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+                }
             }
         }
     }
     __syncthreads();
 
     // Stage 1: 4 -> 4 over the stage-1 brick, origin (od0-1, oh0-1, ow0-1);
-    // runs of 5 along the 10-wide rows.
+    // runs of 5 along the 10-wide rows, all 4 channels per thread (120 runs).
     {
         constexpr int NX = 5, NG = B_W / NX;
-        for (int i = tid; i < 4 * B_D * B_H * NG; i += kThreads) {
-            const int co = i / (B_D * B_H * NG), r0 = i - co * (B_D * B_H * NG);
-            const int z = r0 / (B_H * NG), r = r0 - z * (B_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
-            float acc[NX];
-            conv_run<4, NX>(s_a, A_VOL, A_H, A_W, z, y, x0, sw1 + co * 108, acc);
+        for (int i = tid; i < B_D * B_H * NG; i += kThreads) {
+            const int z = i / (B_H * NG), r = i - z * (B_H * NG), y = r / NG, x0 = (r - y * NG) * NX;
+            float acc[4][NX];
+            conv_run_x4<4, NX>(s_a, A_VOL, A_H, A_W, z, y, x0, s_w1q, acc);
 #pragma unroll
             for (int j = 0; j < NX; ++j) {
-                const float v = __fadd_rn(acc[j], sb1[co]);
                 const bool in_vol = inside(od0 - 1 + z, oh0 - 1 + y, ow0 - 1 + x0 + j, D, H, W);
-                s_b[co * B_VOL + (z * B_H + y) * B_W + x0 + j] = in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+#pragma unroll
+                for (int co = 0; co < 4; ++co) {
+                    const float v = __fadd_rn(acc[co][j], sb1[co]);
+                    s_b[co * B_VOL + (z * B_H + y) * B_W + x0 + j] =
+                        in_vol ? __half2float(__float2half_rn(relu6(v))) : 0.0f;
+                }
             }
         }
     }
     __syncthreads();
 
-    // Stage 2: 4 -> 1, runs of 2 along the 8-wide output rows.
+    // Stage 2: 4 -> 1, blocks of 2 rows x 2 columns per thread (64 threads).
+    // For each (ci, kd) the 4 x 4 input patch is loaded once and serves the
+    // 9 (kh, kw) taps of the 4 outputs; each output's chain still runs in
+    // (ci, kd, kh, kw) order.
     {
-        constexpr int NX = 2, NG = TW / NX;
-        if (tid < TD * TH * NG) {
-            const int z = tid / (TH * NG), r = tid - z * (TH * NG), y = r / NG, x0 = (r - y * NG) * NX;
-            float acc[NX];
-            conv_run<4, NX>(s_b, B_VOL, B_H, B_W, z, y, x0, sw2, acc);
-            const int gd = od0 + z, gh = oh0 + y;
+        constexpr int NX = 2, NY = 2, NG = TW / NX, NYG = TH / NY;
+        if (tid < TD * NYG * NG) {
+            const int z = tid / (NYG * NG), r = tid - z * (NYG * NG), y0 = (r / NG) * NY, x0 = (r % NG) * NX;
+            float acc[NY][NX];
 #pragma unroll
-            for (int j = 0; j < NX; ++j) {
-                const int gw = ow0 + x0 + j;
-                if (gd < D && gh < H && gw < W)
-                    out[i64(b) * vol + (i64(gd) * H + gh) * W + gw] =
-                        __float2half_rn(relu6(__fadd_rn(acc[j], sb2[0])));
-            }
+            for (int a = 0; a < NY; ++a)
+#pragma unroll
+                for (int j = 0; j < NX; ++j) acc[a][j] = 0.0f;
+#pragma unroll
+            for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+                for (int kd = 0; kd < 3; ++kd) {
+                    float patch[NY + 2][NX + 2];
+#pragma unroll
+                    for (int a = 0; a < NY + 2; ++a)
+#pragma unroll
+                        for (int t = 0; t < NX + 2; ++t)
+                            patch[a][t] = s_b[ci * B_VOL + ((z + kd) * B_H + y0 + a) * B_W + x0 + t];
+#pragma unroll
+                    for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                        for (int kw = 0; kw < 3; ++kw) {
+                            const float wv = s_w2[ci * 27 + kd * 9 + kh * 3 + kw];
+#pragma unroll
+                            for (int a = 0; a < NY; ++a)
+#pragma unroll
+                                for (int j = 0; j < NX; ++j) acc[a][j] = __fmaf_rn(patch[a + kh][j + kw], wv, acc[a][j]);
+                        }
+                }
+            const int gd = od0 + z;
+#pragma unroll
+            for (int a = 0; a < NY; ++a)
+#pragma unroll
+                for (int j = 0; j < NX; ++j) {
+                    const int gh = oh0 + y0 + a, gw = ow0 + x0 + j;
+                    if (gd < D && gh < H && gw < W)
+                        out[i64(b) * vol + (i64(gd) * H + gh) * W + gw] =
+                            __float2half_rn(relu6(__fadd_rn(acc[a][j], sb2[0])));
+                }
         }
     }
 }

@@ -263,4 +263,54 @@ int ww_plugin_nv12_decode_enqueue(int out_h, int out_w, const ww_tensor_desc_t* 
     return st == WW_SUCCESS ? 0 : 1;
 }
 
+// ------------------------------------------------------ DisparityRegression
+// No reference counterpart (the reference pipeline ends at CostStem3D); the
+// plugin follows the conventions of the ones above: LINEAR, output dtype =
+// input dtype, 0 / 1 enqueue codes.
+
+// [B, D, H, W] or [B, 1, D, H, W] -> [B, 1, H, W].
+int ww_plugin_disparity_regression_output_dims(int nb_inputs, const ww_tensor_desc_t* inputs,
+                                               ww_tensor_desc_t* out)
+{
+    if (nb_inputs != 1 || inputs == nullptr || out == nullptr) return 1;
+    const ww_tensor_desc_t& d = inputs[0];
+    if (d.nb_dims != 4 && !(d.nb_dims == 5 && d.dims[1] == 1)) return 1;
+    *out = d;
+    out->nb_dims = 4;
+    out->dims[0] = d.dims[0];
+    out->dims[1] = 1;
+    out->dims[2] = d.dims[d.nb_dims - 2];
+    out->dims[3] = d.dims[d.nb_dims - 1];
+    return 0;
+}
+
+// Position 0 fp16 or fp32 LINEAR; the output matches the input's dtype.
+int ww_plugin_disparity_regression_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
+                                                   int nb_outputs)
+{
+    if (in_out == nullptr || nb_inputs != 1 || nb_outputs != 1) return 0;
+    if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
+    const ww_tensor_desc_t& d = in_out[pos];
+    if (d.format != WW_FORMAT_LINEAR) return 0;
+    if (d.dtype != WW_DTYPE_HALF && d.dtype != WW_DTYPE_FLOAT) return 0;
+    return pos == 0 || d.dtype == in_out[0].dtype;
+}
+
+int ww_plugin_disparity_regression_enqueue(int mode, const ww_tensor_desc_t* in_desc,
+                                           const ww_tensor_desc_t* out_desc, const void* const* inputs,
+                                           void* const* outputs, void* stream)
+{
+    if (in_desc == nullptr || out_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    const ww_tensor_desc_t& d = in_desc[0];
+    if (d.nb_dims != 4 && !(d.nb_dims == 5 && d.dims[1] == 1)) return 1;
+    for (int i = 0; i < d.nb_dims; ++i)
+        if (!fits_int(d.dims[i])) return 1;
+    const int n = d.nb_dims;
+    const int st = ww_disparity_regression(inputs[0], outputs[0], d.dtype, out_desc[0].dtype,
+                                           static_cast<int>(d.dims[0]), static_cast<int>(d.dims[n - 3]),
+                                           static_cast<int>(d.dims[n - 2]), static_cast<int>(d.dims[n - 1]), mode,
+                                           stream);
+    return st == WW_SUCCESS ? 0 : 1;
+}
+
 }  // extern "C"

@@ -9,13 +9,14 @@
 // (src/register_plugins.cpp:15-18, the stereo path and the camera decode)
 // under the same names and version -- "CorrVolume" v"1" with field max_disp
 // (default 48), "CostStem3D" v"1" with no required field, "Nv12Decode" v"1"
-// with fields out_h / out_w (224 / 288) -- plus the fused "CorrCostStem3D".  Every method is
+// with fields out_h / out_w (224 / 288) -- plus the fused "CorrCostStem3D" and
+// "DisparityRegression" (field mode), which have no reference counterpart.  Every method is
 // a thin forwarder to the ww_plugin_* functions of the C ABI (plugin_core.cpp),
 // which carry the logic of the reference's IPluginV3 methods
 // (src/plugins/corr_volume/corr_volume.cpp:23-139,
 // src/plugins/cost_stem_3d/cost_stem_3d.cpp:14-97,
 // src/plugins/nv12_decode/nv12_decode.cpp:16-146).  One plugin class serves
-// all three ops; the op kind selects the forwarding target.
+// every op; the op kind selects the forwarding target.
 #include <NvInferRuntime.h>
 #include <NvInferRuntimePlugin.h>
 #include <NvInferPlugin.h>
@@ -32,7 +33,7 @@ namespace ww_trt {
 
 using namespace nvinfer1;
 
-enum class Op { kCorrVolume, kCostStem3D, kCorrCostStem3D, kNv12Decode };
+enum class Op { kCorrVolume, kCostStem3D, kCorrCostStem3D, kNv12Decode, kDisparityRegression };
 
 // Integer fields an op carries; every op stores all three, serialises its own.
 struct Fields {
@@ -41,6 +42,7 @@ struct Fields {
     int32_t act = WW_ACT_RELU;
     int32_t out_h = 224;
     int32_t out_w = 288;
+    int32_t mode = WW_DISP_SOFTARGMAX;
 };
 
 constexpr char const* kVersion = "1";
@@ -52,6 +54,7 @@ char const* op_name(Op op) noexcept
         case Op::kCostStem3D: return "CostStem3D";
         case Op::kCorrCostStem3D: return "CorrCostStem3D";
         case Op::kNv12Decode: return "Nv12Decode";
+        case Op::kDisparityRegression: return "DisparityRegression";
     }
     return "";
 }
@@ -64,6 +67,7 @@ std::vector<char const*> op_fields(Op op)
         case Op::kCostStem3D: return {"act"};
         case Op::kCorrCostStem3D: return {"max_disp", "num_groups", "act"};
         case Op::kNv12Decode: return {"out_h", "out_w"};
+        case Op::kDisparityRegression: return {"mode"};
     }
     return {};
 }
@@ -75,6 +79,7 @@ int32_t* field_slot(Fields& f, char const* name) noexcept
     if (std::strcmp(name, "act") == 0) return &f.act;
     if (std::strcmp(name, "out_h") == 0) return &f.out_h;
     if (std::strcmp(name, "out_w") == 0) return &f.out_w;
+    if (std::strcmp(name, "mode") == 0) return &f.mode;
     return nullptr;
 }
 
@@ -175,6 +180,14 @@ public:
                 out[0].d[2] = eb.constant(mFields.out_h);
                 out[0].d[3] = eb.constant(mFields.out_w);
                 return 0;
+            case Op::kDisparityRegression:  // [B, D, H, W] or [B, 1, D, H, W] -> [B, 1, H, W]
+                if (nbInputs != 1 || (in[0].nbDims != 4 && in[0].nbDims != 5)) return 1;
+                out[0].nbDims = 4;
+                out[0].d[0] = in[0].d[0];
+                out[0].d[1] = eb.constant(1);
+                out[0].d[2] = in[0].d[in[0].nbDims - 2];
+                out[0].d[3] = in[0].d[in[0].nbDims - 1];
+                return 0;
             case Op::kCorrCostStem3D:  // [B, Cout, D, H, W]
                 if (nbInputs != 4 || in[0].nbDims != 4 || in[2].nbDims != 5) return 1;
                 out[0].nbDims = 5;
@@ -204,6 +217,8 @@ public:
                 return ww_plugin_corr_cost_stem3d_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
             case Op::kNv12Decode:
                 return ww_plugin_nv12_decode_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
+            case Op::kDisparityRegression:
+                return ww_plugin_disparity_regression_supports_format(pos, d.data(), nbInputs, nbOutputs) != 0;
         }
         return false;
     }
@@ -244,6 +259,11 @@ public:
                 const ww_tensor_desc_t od = to_ww(outDesc[0]);
                 return ww_plugin_nv12_decode_enqueue(mFields.out_h, mFields.out_w, d.data(), &od, inputs, outputs,
                                                      stream);
+            }
+            case Op::kDisparityRegression: {
+                if (outDesc == nullptr) return 1;
+                const ww_tensor_desc_t od = to_ww(outDesc[0]);
+                return ww_plugin_disparity_regression_enqueue(mFields.mode, d.data(), &od, inputs, outputs, stream);
             }
         }
         return 1;
@@ -331,6 +351,9 @@ struct CorrCostStem3DCreator final : WwCreator {
 struct Nv12DecodeCreator final : WwCreator {
     Nv12DecodeCreator() : WwCreator(Op::kNv12Decode) {}
 };
+struct DisparityRegressionCreator final : WwCreator {
+    DisparityRegressionCreator() : WwCreator(Op::kDisparityRegression) {}
+};
 
 }  // namespace ww_trt
 
@@ -339,9 +362,11 @@ struct Nv12DecodeCreator final : WwCreator {
 using ww_trt::CorrCostStem3DCreator;
 using ww_trt::CorrVolumeCreator;
 using ww_trt::CostStem3DCreator;
+using ww_trt::DisparityRegressionCreator;
 using ww_trt::Nv12DecodeCreator;
 
 REGISTER_TENSORRT_PLUGIN(CorrVolumeCreator);
 REGISTER_TENSORRT_PLUGIN(CostStem3DCreator);
 REGISTER_TENSORRT_PLUGIN(CorrCostStem3DCreator);
 REGISTER_TENSORRT_PLUGIN(Nv12DecodeCreator);
+REGISTER_TENSORRT_PLUGIN(DisparityRegressionCreator);

@@ -22,6 +22,8 @@ Reference plugins (paths relative to the reference project):
   ``num_groups``, ``act``.
 * ``Nv12Decode`` v1, fields ``out_h`` (224), ``out_w`` (288) --
   ``src/plugins/nv12_decode/nv12_decode.cpp:16-146``.
+* ``DisparityRegression`` v1 (extension, no reference counterpart): field
+  ``mode`` (0 soft-argmax, 1 soft-argmin).
 
 Descriptors are :class:`TensorDesc` (dims, dtype, format); dtypes use
 TensorRT's numbering (0 = kFLOAT, 1 = kHALF, 2 = kINT8), format 0 = kLINEAR.
@@ -34,7 +36,7 @@ from dataclasses import dataclass, field
 from . import lib
 
 __all__ = ["TensorDesc", "CorrVolumePlugin", "CostStem3DPlugin", "CorrCostStem3DPlugin", "Nv12DecodePlugin",
-           "PluginCreator", "get_plugin_creator", "registered_creators"]
+           "DisparityRegressionPlugin", "PluginCreator", "get_plugin_creator", "registered_creators"]
 
 DTYPE_FLOAT = 0
 DTYPE_HALF = 1
@@ -252,6 +254,34 @@ class Nv12DecodePlugin(_PluginBase):
                                                    ctypes.c_void_p(_stream(stream)))
 
 
+class DisparityRegressionPlugin(_PluginBase):
+    """``DisparityRegression`` (extension): cost [B, D, H, W] or [B, 1, D, H, W]
+    fp16/fp32 -> disparity [B, 1, H, W] of the same dtype."""
+    NAME = "DisparityRegression"
+
+    def __init__(self, mode: int = 0):
+        super().__init__()
+        self.mode = int(mode)
+
+    def get_fields_to_serialize(self) -> dict:
+        return {"mode": self.mode}
+
+    def get_output_shapes(self, inputs) -> list:
+        out = _Desc()
+        if lib().ww_plugin_disparity_regression_output_dims(len(inputs), _descs(inputs), ctypes.byref(out)) != 0:
+            raise ValueError("DisparityRegression takes one [B, D, H, W] or [B, 1, D, H, W] input")
+        return [TensorDesc._from_c(out).dims]
+
+    def supports_format_combination(self, pos: int, in_out, nb_inputs: int, nb_outputs: int) -> bool:
+        return bool(lib().ww_plugin_disparity_regression_supports_format(pos, _descs(in_out), nb_inputs,
+                                                                         nb_outputs))
+
+    def enqueue(self, input_desc, output_desc, inputs, outputs, stream=None) -> int:
+        return lib().ww_plugin_disparity_regression_enqueue(self.mode, _descs(input_desc), _descs(output_desc),
+                                                            _ptrs(inputs), _ptrs(outputs),
+                                                            ctypes.c_void_p(_stream(stream)))
+
+
 @dataclass
 class PluginCreator:
     """IPluginCreatorV3One counterpart: name, version, field names, create."""
@@ -284,6 +314,7 @@ _CREATORS = {
     ("CostStem3D", "1"): PluginCreator(CostStem3DPlugin, {"act": 0}),
     ("CorrCostStem3D", "1"): PluginCreator(CorrCostStem3DPlugin, {"max_disp": 48, "num_groups": 1, "act": 0}),
     ("Nv12Decode", "1"): PluginCreator(Nv12DecodePlugin, {"out_h": 224, "out_w": 288}),
+    ("DisparityRegression", "1"): PluginCreator(DisparityRegressionPlugin, {"mode": 0}),
 }
 
 

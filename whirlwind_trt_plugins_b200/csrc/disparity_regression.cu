@@ -36,7 +36,7 @@ namespace ww {
 namespace {
 
 constexpr int kChunk = 8;
-constexpr int kBlock = 256;
+constexpr int kBlock = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float ex2_approx(float x)
@@ -246,7 +246,8 @@ __global__ void __launch_bounds__(kBlock) disparity_regression_h4_kernel(const D
     const uint32_t pad = NEG ? 0x7C007C00u : 0xFC00FC00u;  // +inf / -inf half2
     float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     uint64_t s2[2] = {0, 0}, t2[2] = {0, 0};  // (+0, +0) pairs
-    for (int d0 = 0; d0 < p.D; d0 += kChunk) {
+    float fd0 = 0.0f;
+    for (int d0 = 0; d0 < p.D; d0 += kChunk, fd0 += static_cast<float>(kChunk)) {
         uint2 raw[kChunk];
 #pragma unroll
         for (int j = 0; j < kChunk; ++j)
@@ -273,7 +274,7 @@ __global__ void __launch_bounds__(kBlock) disparity_regression_h4_kernel(const D
         t2[1] = mul2(t2[1], f2[1]);
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
-            const float dj = static_cast<float>(d0 + j);
+            const float dj = fd0 + static_cast<float>(j);  // exact; no int -> float conversion (XU pipe)
             const uint64_t d2 = pk(dj, dj);
             const uint64_t e01 = ex2_2(fma2(h2f2(raw[j].x), sl2, nm2[0]));
             const uint64_t e23 = ex2_2(fma2(h2f2(raw[j].y), sl2, nm2[1]));

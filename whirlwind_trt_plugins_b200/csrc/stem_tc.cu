@@ -93,7 +93,13 @@ constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
 constexpr int kMaxVBuf = 3;        // volume row buffers
-constexpr int kDrain = 3;          // M-blocks the epilogue drains before storing them
+// M-blocks the epilogue drains (tensor memory -> registers, slot released)
+// before it stores any of them.  The MMA warp needs every M-block's slot
+// back before the first K-step of the next row, so a row with more M-blocks
+// than this waits for the stores of the first group: with Cout = 16 the
+// packed results are small enough to drain five M-blocks (D <= 80) at once.
+template <int COUTP>
+constexpr int drain_blocks() { return COUTP <= 16 ? 5 : 3; }
 
 struct StemParams {
     const __half* vol;    // volume mode: [B, G, D, H, W]
@@ -729,6 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         // zero the slot, release it with acc_empty), so the MMA warp can
         // start the next row at once; then store them.
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+        constexpr int kDrain = drain_blocks<COUTP>();
         const int rr = warp * 32 + lane;  // M row
         const int w = w0 + (rr & 7);
         const int dsub = rr >> 3;         // 0..15

@@ -59,8 +59,8 @@
 // (nv = 2 or 3 volume buffers: with three, the producers run up to two rows
 // ahead of the MMA warp, which hides the rows they produce while the tensor
 // core's operand reads hold the shared memory.)
-//   acc_full[m]     MMA (commit) -> epilogue    row u-1 of M-block m complete
-//   acc_empty[m]    epilogue -> MMA             row u-1's slot read out
+//   acc_full        MMA (commit) -> epilogue    row u-1 complete in every M-block
+//   acc_empty       epilogue -> MMA             row u-1's slots read out (every M-block)
 // A wait that expires records an error code in the device error word; the
 // waiting role stops, the others run into their own bounded waits, and the
 // CTA winds down and frees its tensor memory.
@@ -567,9 +567,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     uint64_t* final_bar = bars + 2 * kMaxVBuf;
     uint64_t* stage_full = final_bar + 1;             // [n_slots]
     uint64_t* stage_empty = stage_full + p.n_slots;   // [n_slots]
-    uint64_t* acc_full = stage_empty + p.n_slots;     // [n_mb]
-    uint64_t* acc_empty = acc_full + p.n_mb;          // [n_mb]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + p.n_mb);
+    uint64_t* acc_full = stage_empty + p.n_slots;     // one per CTA
+    uint64_t* acc_empty = acc_full + 1;               // one per CTA
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
 
     // ---- set-up: barriers, TMEM, B image, zeroed volume buffers ----
     if (threadIdx.x == 0) {
@@ -582,10 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             mbar_init(smem_addr(&stage_empty[i]), kProdWarps);
         }
         mbar_init(smem_addr(final_bar), 1);
-        for (int m = 0; m < p.n_mb; ++m) {
-            mbar_init(smem_addr(&acc_full[m]), 1);
-            mbar_init(smem_addr(&acc_empty[m]), kEpiWarps);
-        }
+        mbar_init(smem_addr(acc_full), 1);
+        mbar_init(smem_addr(acc_empty), kEpiWarps);
         mbar_fence_init();
     }
     if (warp == kMmaWarp) tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
@@ -746,6 +744,11 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         for (int it = 0; it < n_iter && ok; ++it) {
             const int r = u_first + it - 1;  // output row completed by this volume row
             const int slot = ((r % 3) + 3) % 3;
+            // One commit per row covers every M-block: they complete together
+            // (their last K-step is issued back to back), and a commit per
+            // M-block made the epilogue see them ~0.3-0.5 us apart (measured).
+            if (!warp_wait(smem_addr(acc_full), it & 1, p.err, 1)) break;
+            fence_after_sync();
             for (int m0 = 0; m0 < p.n_mb && ok; m0 += kDrain) {
                 const int mcnt = min(kDrain, p.n_mb - m0);
                 uint32_t ph[kDrain][COUTP / 2];  // fp16 results, packed as (o, o + 1) pairs
@@ -753,8 +756,6 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                 for (int j = 0; j < kDrain; ++j) {
                     if (j >= mcnt) break;
                     const int m = m0 + j;
-                    if (!warp_wait(smem_addr(&acc_full[m]), it & 1, p.err, 1)) { ok = false; break; }
-                    fence_after_sync();
                     uint32_t acc[COUTP];
                     const uint32_t col = lane_base + m * N + slot * COUTP;
 #pragma unroll
@@ -765,11 +766,13 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         for (int q = 0; q < 16; ++q) acc[c + q] = v16[q];
                     }
                     tmem_wait_ld();
-                    // The slot is free once read: the MMA warp restarts it with
-                    // accumulate = 0 (no zeroing here).
-                    fence_before_sync();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_addr(&acc_empty[m]));
+                    // The row's slots are free once read: the MMA warp restarts
+                    // them with accumulate = 0 (no zeroing here).
+                    if (m == p.n_mb - 1) {
+                        fence_before_sync();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_addr(acc_empty));
+                    }
 #pragma unroll
                     for (int k = 0; k < COUTP / 2; ++k) {
                         const float2 bb = *reinterpret_cast<const float2*>(sbias + 2 * k);
@@ -835,10 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             for (int it = 0; it < n_iter; ++it) {
                 const int vb = it % NV;
                 if (!wait_or_fail(smem_addr(&vol_full[vb]), (it / NV) & 1, p.err, 2)) break;
-                bool ok = true;
-                for (int m = 0; m < p.n_mb && it > 0 && ok; ++m)
-                    ok = wait_or_fail(smem_addr(&acc_empty[m]), (it - 1) & 1, p.err, 3);
-                if (!ok) break;
+                if (it > 0 && !wait_or_fail(smem_addr(acc_empty), (it - 1) & 1, p.err, 3)) break;
                 fence_after_sync();
                 const int u = u_first + it;
                 if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     // still holds the row the epilogue drained).
                     issue_row_n<COUTP>(p, tmem_base, a0, b0, (u + 1) % 3);
                 }
-                for (int m = 0; m < p.n_mb; ++m) mma_commit(smem_addr(&acc_full[m]));
+                mma_commit(smem_addr(acc_full));
                 mma_commit(smem_addr(&vol_empty[vb]));
             }
         }
@@ -1105,7 +1105,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
     p.stage_slot_bytes = fused ? ((p.off_l + 8u * Cg * kLRowBytes + 1023) / 1024) * 1024 : 0;
     p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + kLStageW) * 8 * Cg * 2);
-    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 2 * n_mb) * 8 + 16); };
+    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 2) * 8 + 16); };
     auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
         uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
         o = (o + 127) & ~127u;

@@ -233,6 +233,16 @@ __device__ __forceinline__ void transpose8x8(uint32_t (&e)[8], int lane)
     }
 }
 
+// Ties registers written by tcgen05.ld to the point after tcgen05.wait::ld:
+// the empty volatile asm redefines them, so no use can be scheduled above the
+// wait that precedes it.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N])
+{
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // Volume column w' held by row `row` of the correlation tiles: rows 0..7 are
 // w' = 1..8 (the 16-byte aligned staged left columns 8..15, read with
 // ldmatrix), row 8 is w' = 0, row 9 is w' = 9; rows 10..15 are padding.
@@ -752,33 +762,48 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             for (int m0 = 0; m0 < p.n_mb && ok; m0 += kDrain) {
                 const int mcnt = min(kDrain, p.n_mb - m0);
                 uint32_t ph[kDrain][COUTP / 2];  // fp16 results, packed as (o, o + 1) pairs
+                // With Cout = 16, M-blocks in pairs: both tensor-memory loads
+                // in flight behind one wait (each wait costs a load latency);
+                // with Cout = 32 a pair's registers would spill.
+                constexpr int kPair = COUTP <= 16 ? 2 : 1;
 #pragma unroll
-                for (int j = 0; j < kDrain; ++j) {
+                for (int j = 0; j < kDrain; j += kPair) {
                     if (j >= mcnt) break;
-                    const int m = m0 + j;
-                    uint32_t acc[COUTP];
-                    const uint32_t col = lane_base + m * N + slot * COUTP;
+                    const bool two = kPair == 2 && j + 1 < mcnt;
+                    uint32_t acc[kPair][COUTP];
 #pragma unroll
-                    for (int c = 0; c < COUTP; c += 16) {
-                        uint32_t v16[16];
-                        tmem_ld16(col + c, v16);
+                    for (int h = 0; h < kPair; ++h) {
+                        if (h == 1 && !two) break;
+                        const uint32_t col = lane_base + (m0 + j + h) * N + slot * COUTP;
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) acc[c + q] = v16[q];
+                        for (int c = 0; c < COUTP; c += 16) {
+                            uint32_t v16[16];
+                            tmem_ld16(col + c, v16);
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) acc[h][c + q] = v16[q];
+                        }
                     }
                     tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < kPair; ++h) reg_fence(acc[h]);  // no use of acc above the wait
                     // The row's slots are free once read: the MMA warp restarts
                     // them with accumulate = 0 (no zeroing here).
-                    if (m == p.n_mb - 1) {
+                    if (m0 + j + (two ? 1 : 0) == p.n_mb - 1) {
                         fence_before_sync();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(acc_empty));
                     }
 #pragma unroll
-                    for (int k = 0; k < COUTP / 2; ++k) {
-                        const float2 bb = *reinterpret_cast<const float2*>(sbias + 2 * k);
-                        const __half2 h2 = __floats2half2_rn(act_apply(__uint_as_float(acc[2 * k]) + bb.x, p.act),
-                                                             act_apply(__uint_as_float(acc[2 * k + 1]) + bb.y, p.act));
-                        ph[j][k] = *reinterpret_cast<const uint32_t*>(&h2);
+                    for (int h = 0; h < kPair; ++h) {
+                        if (h == 1 && !two) break;
+#pragma unroll
+                        for (int k = 0; k < COUTP / 2; ++k) {
+                            const float2 bb = *reinterpret_cast<const float2*>(sbias + 2 * k);
+                            const __half2 h2 =
+                                __floats2half2_rn(act_apply(__uint_as_float(acc[h][2 * k]) + bb.x, p.act),
+                                                  act_apply(__uint_as_float(acc[h][2 * k + 1]) + bb.y, p.act));
+                            ph[j + h][k] = *reinterpret_cast<const uint32_t*>(&h2);
+                        }
                     }
                 }
                 if (!ok || r < r0 || r >= r1) continue;  // warp-uniform

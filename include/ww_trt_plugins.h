@@ -139,6 +139,19 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
                              void* stream);
 
 /* ---------------------------------------------------------------------------
+ * CorrVolume (G = 1) fused with the reference's 3-stage CostStem3D, the pair
+ * the reference runs at its native shape ([1, 1, 48, 32, 40]):
+ *   out = ww_cost_stem3d_ref3(ww_corr_volume(left, right, D), w0 .. b2)
+ * bit for bit (the correlation is computed inside the stem's bricks with the
+ * same arithmetic and scale rule; the volume never reaches device memory).
+ * left, right : [B, C, H, W] fp16; weights as ww_cost_stem3d_ref3;
+ * out         : [B, 1, D, H, W] fp16.
+ * ------------------------------------------------------------------------- */
+int ww_corr_cost_stem3d_ref3(const void* left, const void* right, void* out, const void* w0, const void* b0,
+                             const void* w1, const void* b1, const void* w2, const void* b2, int B, int C, int H,
+                             int W, int D, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Nv12Decode: NV12 -> planar RGB in [-1, 1], bilinear resize.
  * nv12 : [B, H_IN * 3 / 2, W_IN] uint8 (Y plane, then interleaved U/V rows
  *        at half resolution); out : [B, 3, H_OUT, W_OUT], dtype
@@ -215,7 +228,9 @@ int ww_plugin_cost_stem3d_enqueue(int nb_inputs, int act, const ww_tensor_desc_t
 
 /* "CorrCostStem3D" v"1" (extension): fields max_disp (48), num_groups (1),
  * act (0 ReLU, 1 ReLU6); inputs left, right [B,C,H,W], w [Cout,G,3,3,3], b [Cout];
- * output [B, Cout, max_disp, H, W]; fp16 only. */
+ * output [B, Cout, max_disp, H, W]; fp16 only.  With 8 inputs (left, right,
+ * w0, b0, w1, b1, w2, b2; num_groups 1) it is ww_corr_cost_stem3d_ref3 and
+ * the output is [B, 1, max_disp, H, W]. */
 int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_inputs,
                                            const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out);
 int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out,

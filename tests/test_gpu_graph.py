@@ -27,6 +27,7 @@ def test_front_end_captures_and_replays():
         "nv12": torch.empty((2, 3, 60, 80), dtype=torch.float16, device="cuda"),
         "stem3": torch.empty_like(vol1),
         "disp": torch.empty((2, 1, 10, 16), dtype=torch.float16, device="cuda"),
+        "corr_stem3": torch.empty((B, 1, cfg.D, H, W), dtype=torch.float16, device="cuda"),
     }
 
     def run():
@@ -35,6 +36,7 @@ def test_front_end_captures_and_replays():
         ww.nv12_decode(frames, 60, 80, out=outs["nv12"])
         ww.cost_stem3d_ref3(vol1, *ws, out=outs["stem3"])
         ww.disparity_regression(agg, ww.DISP_SOFTARGMIN, out=outs["disp"])
+        ww.corr_cost_stem3d_ref3(L, R, *ws, max_disp=cfg.D, out=outs["corr_stem3"])
 
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())

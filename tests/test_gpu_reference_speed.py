@@ -8,7 +8,9 @@ baseline the reference would give on this hardware.
   the fused ww_corr_cost_stem3d, which also runs the G -> Cout stem the
   reference has no kernel for.
 * The reference CostStem3D at its native shape [1, 1, 48, 32, 40] against
-  ww_cost_stem3d_ref3 (bit-identical output).
+  ww_cost_stem3d_ref3 (bit-identical output), and the reference's
+  CorrVolume -> CostStem3D pair at that shape against the fused
+  ww_corr_cost_stem3d_ref3 (bit-identical output).
 * The reference Nv12Decode (one launch per frame, as its launcher takes one
   image) on 8 720p frames -> 224 x 288 fp16 against one ww_nv12_decode call
   (bit-identical output).
@@ -169,6 +171,49 @@ def test_native_stem_vs_reference_kernel(env):
           f"  per call: {c_ref:.2f} | {c_ours:.2f} us")
     _save()
     assert t_ours < t_ref
+
+
+def test_native_corr_stem_vs_reference_pair(env):
+    """The reference's own pair at its native shape (CorrVolume, then the
+    3-stage CostStem3D on [1, 1, 48, 32, 40]; C = 64 features) against the
+    fused ww_corr_cost_stem3d_ref3 and against this library's two-call pair."""
+    torch, ww, ref = env
+    g = torch.Generator(device="cuda").manual_seed(11)
+    B, C, H, W, D = 1, 64, 32, 40, 48
+    L = torch.randn((B, C, H, W), generator=g, device="cuda").half()
+    R = torch.randn((B, C, H, W), generator=g, device="cuda").half()
+    ws = [(torch.randn((n,), generator=g, device="cuda") * s).half()
+          for n, s in ((108, 0.2), (4, 0.1), (432, 0.2), (4, 0.1), (108, 0.2), (1, 0.1))]
+    vol_ref = torch.empty((B, D, H, W), dtype=torch.float16, device="cuda")
+    o_ref = torch.empty((B, 1, D, H, W), dtype=torch.float16, device="cuda")
+    vol = torch.empty((B, D, H, W), dtype=torch.float16, device="cuda")
+    o_pair = torch.empty_like(o_ref)
+    o = torch.empty_like(o_ref)
+
+    def run_ref():
+        s = torch.cuda.current_stream().cuda_stream
+        assert ref.wwref_corr_volume_f16(L.data_ptr(), R.data_ptr(), vol_ref.data_ptr(), B, C, H, W, D, s) == 0
+        assert ref.wwref_cost_stem3d(vol_ref.data_ptr(), o_ref.data_ptr(), *[w.data_ptr() for w in ws], B, D, H, W,
+                                     s) == 0
+
+    def run_pair():
+        ww.corr_volume(L, R, D, out=vol)
+        ww.cost_stem3d_ref3(vol.unsqueeze(1), *ws, out=o_pair)
+
+    def run_fused():
+        ww.corr_cost_stem3d_ref3(L, R, *ws, max_disp=D, out=o)
+
+    t_ref, t_pair, t_fused = _device_us(torch, run_ref), _device_us(torch, run_pair), _device_us(torch, run_fused)
+    c_ref, c_pair, c_fused = _median_us(torch, run_ref), _median_us(torch, run_pair), _median_us(torch, run_fused)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref) and torch.equal(o_pair, o_ref)
+    RESULTS["corr_stem3_native"] = {"reference_pair_device_us": t_ref, "ww_pair_device_us": t_pair,
+                                    "ww_fused_device_us": t_fused, "reference_pair_call_us": c_ref,
+                                    "ww_pair_call_us": c_pair, "ww_fused_call_us": c_fused}
+    print(f"\nnative CorrVolume -> CostStem3D (C = 64) device: reference pair {t_ref:.2f} us | ww pair {t_pair:.2f} us"
+          f" | ww fused {t_fused:.2f} us;  per call: {c_ref:.2f} | {c_pair:.2f} | {c_fused:.2f} us")
+    _save()
+    assert t_fused < t_ref
 
 
 def test_nv12_decode_vs_reference_kernel(env):

@@ -13,6 +13,8 @@ reference project):
   (``src/plugins/corr_volume/corr_volume_kernel.hpp:17-27``)
 * ``cost_stem3d_ref3(vol, w0, b0, w1, b1, w2, b2)``     -- CostStem3D 7-input form
   (``src/plugins/cost_stem_3d/cost_stem_3d_kernel.hpp:17-30``)
+* ``corr_cost_stem3d_ref3(left, right, w0..b2, max_disp)`` -- CorrVolume (G = 1)
+  fused with the reference CostStem3D, bit-identical to the pair
 * ``cost_stem3d(vol, w, b, act)``                      -- generalised 3-input stem
 * ``corr_cost_stem3d(left, right, w, b, max_disp, num_groups, act)`` -- fused op
 * ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
@@ -31,7 +33,7 @@ import ctypes
 import os
 
 __all__ = [
-    "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "cost_stem3d",
+    "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "corr_cost_stem3d_ref3", "cost_stem3d",
     "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "disparity_regression", "fold_bn", "device_error",
     "clear_device_error", "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF", "DISP_SOFTARGMAX", "DISP_SOFTARGMIN",
 ]
@@ -70,6 +72,7 @@ def _load() -> ctypes.CDLL:
     L.ww_abi_version.restype = i
     L.ww_corr_volume.argtypes = [p, p, p] + [i] * 7 + [p]
     L.ww_cost_stem3d_ref3.argtypes = [p] * 8 + [i] * 4 + [p]
+    L.ww_corr_cost_stem3d_ref3.argtypes = [p] * 9 + [i] * 5 + [p]
     L.ww_cost_stem3d.argtypes = [p, p, p, p] + [i] * 7 + [p]
     L.ww_corr_cost_stem3d.argtypes = [p, p, p, p, p] + [i] * 8 + [p]
     L.ww_corr_cost_stem3d_band.argtypes = [p, p, p, p, p] + [i] * 12 + [p]
@@ -158,6 +161,29 @@ def cost_stem3d_ref3(vol, w0, b0, w1, b1, w2, b2, out=None, stream=None):
     _check("ww_cost_stem3d_ref3", _lib.ww_cost_stem3d_ref3(vol.data_ptr(), out.data_ptr(),
                                                            *[x.data_ptr() for x in ws], B, D, H, W,
                                                            _stream_ptr(stream)))
+    return out
+
+
+def corr_cost_stem3d_ref3(left, right, w0, b0, w1, b1, w2, b2, max_disp: int = 48, out=None, stream=None):
+    """CorrVolume (G = 1) fused with the reference CostStem3D (1->4->4->1,
+    ReLU6): bit-identical to cost_stem3d_ref3(corr_volume(left, right,
+    max_disp)); left, right [B, C, H, W] fp16 -> [B, 1, max_disp, H, W] fp16."""
+    torch = _torch()
+    _dev(left, "left", torch.float16)
+    _dev(right, "right", torch.float16)
+    if left.dim() != 4 or left.shape != right.shape:
+        raise ValueError("left and right must both be [B, C, H, W]")
+    ws = [_dev(x, n, torch.float16) for x, n in zip((w0, b0, w1, b1, w2, b2), ("w0", "b0", "w1", "b1", "w2", "b2"))]
+    for x, n in zip(ws, (108, 4, 432, 4, 108, 1)):
+        if x.numel() != n:
+            raise ValueError("CostStem3D weight/bias has the wrong size")
+    B, C, H, W = left.shape
+    if out is None:
+        out = torch.empty((B, 1, max_disp, H, W), dtype=torch.float16, device=left.device)
+    _dev(out, "out", torch.float16)
+    _check("ww_corr_cost_stem3d_ref3", _lib.ww_corr_cost_stem3d_ref3(
+        left.data_ptr(), right.data_ptr(), out.data_ptr(), *[x.data_ptr() for x in ws], B, C, H, W, max_disp,
+        _stream_ptr(stream)))
     return out
 
 

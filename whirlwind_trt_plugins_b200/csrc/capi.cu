@@ -11,6 +11,9 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
 int cost_stem3d_ref3_launch(const void* in, void* out, const void* w0, const void* b0,
                             const void* w1, const void* b1, const void* w2, const void* b2,
                             int B, int D, int H, int W, cudaStream_t stream) noexcept;
+int corr_cost_stem3d_ref3_launch(const void* left, const void* right, void* out, const void* w0, const void* b0,
+                                 const void* w1, const void* b1, const void* w2, const void* b2, int B, int C,
+                                 int H, int W, int D, cudaStream_t stream) noexcept;
 int stem_tc_launch(const void* vol, const void* left, const void* right, const void* w,
                    const void* b, void* out, int B, int C, int G, int H, int W, int D, int Cout,
                    int act, int in_row0, int in_rows, int out_row0, int out_rows,
@@ -132,6 +135,14 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
     if (left == nullptr || right == nullptr) return WW_ERR_NULL_POINTER;
     return ww::stem_tc_launch(nullptr, left, right, w, b, out, B, C, G, H, W, D, Cout, act, in_row0,
                               in_rows, out_row0, out_rows, static_cast<cudaStream_t>(stream));
+}
+
+int ww_corr_cost_stem3d_ref3(const void* left, const void* right, void* out, const void* w0, const void* b0,
+                             const void* w1, const void* b1, const void* w2, const void* b2, int B, int C, int H,
+                             int W, int D, void* stream)
+{
+    return ww::corr_cost_stem3d_ref3_launch(left, right, out, w0, b0, w1, b1, w2, b2, B, C, H, W, D,
+                                            static_cast<cudaStream_t>(stream));
 }
 
 int ww_nv12_decode(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT, int W_OUT,

@@ -89,33 +89,56 @@ __device__ __forceinline__ void conv_run_x4(const float* src, int cs, int SH, in
             }
 }
 
-__global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
-    const __half* __restrict__ in, __half* __restrict__ out,
-    const __half* __restrict__ w0, const __half* __restrict__ b0,
-    const __half* __restrict__ w1, const __half* __restrict__ b1,
-    const __half* __restrict__ w2, const __half* __restrict__ b2,
-    int D, int H, int W, int n_dtiles)
+struct Ref3Params {
+    const __half* in;     // stem input [B, 1, D, H, W] (CORR = false)
+    const __half* left;   // features [B, C, H, W] (CORR = true)
+    const __half* right;
+    __half* out;          // [B, 1, D, H, W]
+    const __half *w0, *b0, *w1, *b1, *w2, *b2;
+    int C, D, H, W, n_dtiles;
+    int scale_div;        // correlation scale rule: 1 acc / C, 0 acc * (1 / C)
+    float inv_c;
+};
+
+// Correlation staging (CORR = true): per chunk of kCorrC channels the left
+// rows [c][14 rows][14 cols] and the right rows [c][14 rows][23 cols] of the
+// brick, fp16, in the space of the two intermediate bricks (free until
+// stage 0).  A thread issues all kStageIt of its loads of a chunk before it
+// stores any (one memory latency per chunk, not one per load).
+constexpr int kCorrC = 16;
+constexpr int kLTile = I_H * I_W;        // 196
+constexpr int kRW = I_W + I_D - 1;       // 23 right columns: w - d over the brick
+constexpr int kRTile = I_H * kRW;        // 322
+constexpr int kStageIt = (kCorrC * (kLTile + kRTile) + kThreads - 1) / kThreads;
+static_assert(kCorrC * (kLTile + kRTile) * 2 <= (4 * A_VOL + 4 * B_VOL) * 4,
+              "correlation tiles exceed the brick space");
+
+template <bool CORR>
+__global__ void __launch_bounds__(kThreads, CORR ? 2 : 4) cost_stem3d_ref3_kernel(const Ref3Params p)
 {
     __shared__ float s_in[I_VOL];
-    __shared__ float s_a[4 * A_VOL];
-    __shared__ float s_b[4 * B_VOL];
+    __shared__ float s_ab[4 * A_VOL + 4 * B_VOL];
     __shared__ float4 s_w0q[27];       // [tap] -> 4 output channels
     __shared__ float4 s_w1q[4 * 27];   // [ci][tap] -> 4 output channels
     __shared__ float s_w2[108];        // [ci][tap]
     __shared__ float s_bias[9];        // b0[4], b1[4], b2
+    float* s_a = s_ab;
+    float* s_b = s_ab + 4 * A_VOL;
     float* sw0q = reinterpret_cast<float*>(s_w0q);
     float* sw1q = reinterpret_cast<float*>(s_w1q);
     const float* sb0 = s_bias;
     const float* sb1 = s_bias + 4;
     const float* sb2 = s_bias + 8;
+    const __half *w0 = p.w0, *b0 = p.b0, *w1 = p.w1, *b1 = p.b1, *w2 = p.w2, *b2 = p.b2;
+    __half* out = p.out;
+    const int D = p.D, H = p.H, W = p.W;
 
     const int tid = threadIdx.x;
-    const int b = blockIdx.z / n_dtiles;
-    const int od0 = (blockIdx.z - b * n_dtiles) * TD;
+    const int b = blockIdx.z / p.n_dtiles;
+    const int od0 = (blockIdx.z - b * p.n_dtiles) * TD;
     const int oh0 = blockIdx.y * TH;
     const int ow0 = blockIdx.x * TW;
     const int64_t vol = i64(D) * H * W;
-    const __half* src = in + i64(b) * vol;
 
     // w0 [co][27] -> s_w0q[tap].co; w1 [co][ci][27] -> s_w1q[ci * 27 + tap].co.
     // All of a thread's global loads are issued before its first shared store.
@@ -151,7 +174,8 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
         }
     }
     // Input brick, origin (od0-3, oh0-3, ow0-3), zero outside the volume.
-    {
+    if constexpr (!CORR) {
+        const __half* src = p.in + i64(b) * vol;
         constexpr int kIt = (I_VOL + kThreads - 1) / kThreads;
         __half v[kIt];
 #pragma unroll
@@ -166,6 +190,74 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
         for (int k = 0; k < kIt; ++k) {
             const int i = tid + k * kThreads;
             if (i < I_VOL) s_in[i] = __half2float(v[k]);
+        }
+    } else {
+        // The brick is the correlation volume itself, computed here with the
+        // arithmetic of the bit-exact correlation kernel: per value an fp32
+        // fma chain over the channels in order from +0, then acc / C or
+        // acc * (1 / C) (the reference's rule for this call), fp16 rounding;
+        // +0 where w - d < 0.  Thread (y, x) < (14, 14) owns the brick's 10
+        // disparities at that position: one left value and 10 right values
+        // (a contiguous run of the right row) per channel.
+        __half* Lt = reinterpret_cast<__half*>(s_ab);  // [kCorrC][14][14]
+        __half* Rt = Lt + kCorrC * kLTile;             // [kCorrC][14][23]
+        const int rw0 = ow0 - od0 - 9;         // image column of right-tile column 0
+        const int64_t plane = i64(H) * W;
+        const __half* lsrc = p.left + i64(b) * p.C * plane;
+        const __half* rsrc = p.right + i64(b) * p.C * plane;
+        const int y = tid / I_W, x = tid - y * I_W;  // valid for tid < 196
+        float acc[I_D];
+#pragma unroll
+        for (int z = 0; z < I_D; ++z) acc[z] = 0.0f;
+        for (int c0 = 0; c0 < p.C; c0 += kCorrC) {
+            const int nc = min(kCorrC, p.C - c0);
+            const int n_l = nc * kLTile, n_all = nc * (kLTile + kRTile);
+            __half v[kStageIt];
+#pragma unroll
+            for (int k = 0; k < kStageIt; ++k) {
+                const int i = tid + k * kThreads;
+                v[k] = __float2half_rn(0.0f);
+                if (i < n_l) {
+                    const int c = i / kLTile, r = i - c * kLTile, yy = r / I_W, xx = r - yy * I_W;
+                    const int gh = oh0 - 3 + yy, gw = ow0 - 3 + xx;
+                    if (gh >= 0 && gh < H && gw >= 0 && gw < W) v[k] = lsrc[i64(c0 + c) * plane + i64(gh) * W + gw];
+                } else if (i < n_all) {
+                    const int q = i - n_l;
+                    const int c = q / kRTile, r = q - c * kRTile, yy = r / kRW, xx = r - yy * kRW;
+                    const int gh = oh0 - 3 + yy, gw = rw0 + xx;
+                    if (gh >= 0 && gh < H && gw >= 0 && gw < W) v[k] = rsrc[i64(c0 + c) * plane + i64(gh) * W + gw];
+                }
+            }
+            __syncthreads();  // the previous chunk's tiles are consumed
+#pragma unroll
+            for (int k = 0; k < kStageIt; ++k) {
+                const int i = tid + k * kThreads;
+                if (i < n_l) Lt[i] = v[k];
+                else if (i < n_all) Rt[i - n_l] = v[k];
+            }
+            __syncthreads();
+            if (tid < kLTile) {
+                for (int c = 0; c < nc; ++c) {
+                    const float lv = __half2float(Lt[c * kLTile + tid]);
+                    // right column of disparity z: (x - z) + 9
+                    const __half* rrow = Rt + c * kRTile + y * kRW + x;
+#pragma unroll
+                    for (int z = 0; z < I_D; ++z) acc[z] = __fmaf_rn(lv, __half2float(rrow[9 - z]), acc[z]);
+                }
+            }
+        }
+        if (tid < kLTile) {
+            const float cf = static_cast<float>(p.C);
+#pragma unroll
+            for (int z = 0; z < I_D; ++z) {
+                const int gd = od0 - 3 + z, gh = oh0 - 3 + y, gw = ow0 - 3 + x;
+                float v = 0.0f;
+                if (inside(gd, gh, gw, D, H, W) && gw >= gd) {
+                    const float sc = p.scale_div ? __fdiv_rn(acc[z], cf) : __fmul_rn(acc[z], p.inv_c);
+                    v = __half2float(__float2half_rn(sc));
+                }
+                s_in[(z * I_H + y) * I_W + x] = v;
+            }
         }
     }
     __syncthreads();
@@ -264,22 +356,70 @@ __global__ void __launch_bounds__(kThreads) cost_stem3d_ref3_kernel(
 
 }  // namespace
 
+int corr_scale_div(bool is_half, int B, int C, int H, int W, int D, int sm_count) noexcept;
+
+namespace {
+
+int ref3_launch(bool corr, Ref3Params& p, int B, cudaStream_t stream, const char* name) noexcept
+{
+    if (!p.w0 || !p.b0 || !p.w1 || !p.b1 || !p.w2 || !p.b2 || !p.out) return WW_ERR_NULL_POINTER;
+    if (B < 0 || p.D < 0 || p.H < 0 || p.W < 0 || p.C < 0) return WW_ERR_INVALID_SHAPE;
+    if (B == 0 || p.D == 0 || p.H == 0 || p.W == 0) return WW_SUCCESS;
+    if (corr && p.C == 0) return WW_ERR_INVALID_SHAPE;
+    p.n_dtiles = (p.D + TD - 1) / TD;
+    if (static_cast<long long>(B) * p.n_dtiles > 65535 || (p.H + TH - 1) / TH > 65535) return WW_ERR_UNSUPPORTED;
+    DeviceInfo dev;
+    if (current_device_info(&dev) != WW_SUCCESS) return WW_ERR_DEVICE;
+    if (corr) {
+        p.scale_div = corr_scale_div(true, B, p.C, p.H, p.W, p.D, dev.sm_count);
+        p.inv_c = 1.0f / static_cast<float>(p.C);
+    }
+    dim3 grid((p.W + TW - 1) / TW, (p.H + TH - 1) / TH, B * p.n_dtiles);
+    if (corr) cost_stem3d_ref3_kernel<true><<<grid, kThreads, 0, stream>>>(p);
+    else cost_stem3d_ref3_kernel<false><<<grid, kThreads, 0, stream>>>(p);
+    return launch_status(name);
+}
+
+Ref3Params ref3_params(void* out, const void* w0, const void* b0, const void* w1, const void* b1, const void* w2,
+                       const void* b2, int D, int H, int W) noexcept
+{
+    auto h = [](const void* q) { return static_cast<const __half*>(q); };
+    Ref3Params p{};
+    p.out = static_cast<__half*>(out);
+    p.w0 = h(w0);
+    p.b0 = h(b0);
+    p.w1 = h(w1);
+    p.b1 = h(b1);
+    p.w2 = h(w2);
+    p.b2 = h(b2);
+    p.D = D;
+    p.H = H;
+    p.W = W;
+    return p;
+}
+
+}  // namespace
+
 int cost_stem3d_ref3_launch(const void* in, void* out, const void* w0, const void* b0,
                             const void* w1, const void* b1, const void* w2, const void* b2,
                             int B, int D, int H, int W, cudaStream_t stream) noexcept
 {
-    if (!in || !out || !w0 || !b0 || !w1 || !b1 || !w2 || !b2) return WW_ERR_NULL_POINTER;
-    if (B < 0 || D < 0 || H < 0 || W < 0) return WW_ERR_INVALID_SHAPE;
-    if (B == 0 || D == 0 || H == 0 || W == 0) return WW_SUCCESS;
-    const int n_dtiles = (D + TD - 1) / TD;
-    if (static_cast<long long>(B) * n_dtiles > 65535 || (H + TH - 1) / TH > 65535) return WW_ERR_UNSUPPORTED;
-    DeviceInfo dev;
-    if (current_device_info(&dev) != WW_SUCCESS) return WW_ERR_DEVICE;
-    dim3 grid((W + TW - 1) / TW, (H + TH - 1) / TH, B * n_dtiles);
-    auto h = [](const void* p) { return static_cast<const __half*>(p); };
-    cost_stem3d_ref3_kernel<<<grid, kThreads, 0, stream>>>(h(in), static_cast<__half*>(out), h(w0), h(b0),
-                                                           h(w1), h(b1), h(w2), h(b2), D, H, W, n_dtiles);
-    return launch_status("ww_cost_stem3d_ref3");
+    if (!in) return WW_ERR_NULL_POINTER;
+    Ref3Params p = ref3_params(out, w0, b0, w1, b1, w2, b2, D, H, W);
+    p.in = static_cast<const __half*>(in);
+    return ref3_launch(false, p, B, stream, "ww_cost_stem3d_ref3");
+}
+
+int corr_cost_stem3d_ref3_launch(const void* left, const void* right, void* out, const void* w0, const void* b0,
+                                 const void* w1, const void* b1, const void* w2, const void* b2, int B, int C,
+                                 int H, int W, int D, cudaStream_t stream) noexcept
+{
+    if (!left || !right) return WW_ERR_NULL_POINTER;
+    Ref3Params p = ref3_params(out, w0, b0, w1, b1, w2, b2, D, H, W);
+    p.left = static_cast<const __half*>(left);
+    p.right = static_cast<const __half*>(right);
+    p.C = C;
+    return ref3_launch(true, p, B, stream, "ww_corr_cost_stem3d_ref3");
 }
 
 }  // namespace ww

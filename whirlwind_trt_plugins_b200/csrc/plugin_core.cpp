@@ -164,12 +164,15 @@ int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_
                                            const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
 {
     (void)num_groups;
-    if (nb_inputs != 4 || inputs == nullptr || out == nullptr) return 1;
-    if (inputs[0].nb_dims != 4 || inputs[2].nb_dims != 5) return 1;
+    if ((nb_inputs != 4 && nb_inputs != 8) || inputs == nullptr || out == nullptr) return 1;
+    if (inputs[0].nb_dims != 4) return 1;
+    if (nb_inputs == 4 && inputs[2].nb_dims != 5) return 1;
     *out = inputs[0];
     out->nb_dims = 5;
     out->dims[0] = inputs[0].dims[0];
-    out->dims[1] = inputs[2].dims[0];
+    // 8 inputs: the reference's 3-stage stem (w0, b0, w1, b1, w2, b2), one
+    // output channel
+    out->dims[1] = nb_inputs == 8 ? 1 : inputs[2].dims[0];
     out->dims[2] = max_disp;
     out->dims[3] = inputs[0].dims[2];
     out->dims[4] = inputs[0].dims[3];
@@ -179,7 +182,7 @@ int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_
 int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out, int nb_inputs,
                                                int nb_outputs)
 {
-    if (in_out == nullptr || nb_inputs != 4 || nb_outputs != 1) return 0;
+    if (in_out == nullptr || (nb_inputs != 4 && nb_inputs != 8) || nb_outputs != 1) return 0;
     if (pos < 0 || pos >= nb_inputs + nb_outputs) return 0;
     return is_linear_half(in_out[pos]);
 }
@@ -189,10 +192,21 @@ int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act, co
 {
     if (in_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
     const ww_tensor_desc_t& d = in_desc[0];
-    const ww_tensor_desc_t& wd = in_desc[2];
-    if (d.nb_dims != 4 || wd.nb_dims != 5) return 1;
+    if (d.nb_dims != 4) return 1;
     for (int i = 0; i < 4; ++i)
         if (!fits_int(d.dims[i])) return 1;
+    if (d.dtype != WW_DTYPE_HALF) return 1;
+    if (in_desc[2].nb_dims != 5) {
+        // 8 inputs: CorrVolume (G = 1) fused with the reference's 3-stage
+        // CostStem3D; num_groups must be 1 and act is ReLU6 by definition.
+        if (num_groups > 1) return 1;
+        const int st = ww_corr_cost_stem3d_ref3(inputs[0], inputs[1], outputs[0], inputs[2], inputs[3], inputs[4],
+                                                inputs[5], inputs[6], inputs[7], static_cast<int>(d.dims[0]),
+                                                static_cast<int>(d.dims[1]), static_cast<int>(d.dims[2]),
+                                                static_cast<int>(d.dims[3]), max_disp, stream);
+        return st == WW_SUCCESS ? 0 : 1;
+    }
+    const ww_tensor_desc_t& wd = in_desc[2];
     const int G = num_groups <= 0 ? 1 : num_groups;
     if (wd.dims[1] != G || wd.dims[2] != 3 || wd.dims[3] != 3 || wd.dims[4] != 3 || !fits_int(wd.dims[0])) return 1;
     if (d.dtype != WW_DTYPE_HALF) return 1;

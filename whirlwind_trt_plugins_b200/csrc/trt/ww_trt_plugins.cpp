@@ -188,11 +188,12 @@ public:
                 out[0].d[2] = in[0].d[in[0].nbDims - 2];
                 out[0].d[3] = in[0].d[in[0].nbDims - 1];
                 return 0;
-            case Op::kCorrCostStem3D:  // [B, Cout, D, H, W]
-                if (nbInputs != 4 || in[0].nbDims != 4 || in[2].nbDims != 5) return 1;
+            case Op::kCorrCostStem3D:  // [B, Cout, D, H, W]; 8 inputs (3-stage stem): Cout = 1
+                if ((nbInputs != 4 && nbInputs != 8) || in[0].nbDims != 4) return 1;
+                if (nbInputs == 4 && in[2].nbDims != 5) return 1;
                 out[0].nbDims = 5;
                 out[0].d[0] = in[0].d[0];
-                out[0].d[1] = in[2].d[0];
+                out[0].d[1] = nbInputs == 8 ? eb.constant(1) : in[2].d[0];
                 out[0].d[2] = eb.constant(mFields.max_disp);
                 out[0].d[3] = in[0].d[2];
                 out[0].d[4] = in[0].d[3];
@@ -205,8 +206,8 @@ public:
                                    int32_t nbOutputs) noexcept override
     {
         const int n = nbInputs + nbOutputs;
-        if (n <= 0 || n > 8) return false;
-        std::array<ww_tensor_desc_t, 8> d{};
+        if (n <= 0 || n > 9) return false;  // up to 8 inputs + 1 output
+        std::array<ww_tensor_desc_t, 9> d{};
         for (int i = 0; i < n; ++i) d[i] = to_ww(inOut[i].desc);
         switch (mOp) {
             case Op::kCorrVolume:
@@ -240,10 +241,10 @@ public:
     int32_t enqueue(PluginTensorDesc const* inDesc, PluginTensorDesc const* outDesc, void const* const* inputs,
                     void* const* outputs, void*, cudaStream_t stream) noexcept override
     {
-        // Descriptors of the inputs: 2 (CorrVolume), 7 or 3 (CostStem3D), 4 (fused).
-        std::array<ww_tensor_desc_t, 7> d{};
+        // Descriptors of the inputs: 2 (CorrVolume), 7 or 3 (CostStem3D), 4 or 8 (fused).
+        std::array<ww_tensor_desc_t, 8> d{};
         const int nin = mNbInputs;
-        if (nin < 1 || nin > 7) return 1;
+        if (nin < 1 || nin > 8) return 1;
         for (int i = 0; i < nin; ++i) d[i] = to_ww(inDesc[i]);
         switch (mOp) {
             case Op::kCorrVolume:

@@ -191,7 +191,10 @@ class CostStem3DPlugin(_PluginBase):
 
 
 class CorrCostStem3DPlugin(_PluginBase):
-    """``CorrCostStem3D`` (extension): CorrVolume fused with a G -> Cout stem."""
+    """``CorrCostStem3D`` (extension): CorrVolume fused with a G -> Cout stem
+    (inputs left, right, w, b); with 8 inputs (left, right, w0, b0, w1, b1,
+    w2, b2; num_groups 1) CorrVolume fused with the reference's 3-stage
+    CostStem3D, bit-identical to the CorrVolume -> CostStem3D pair."""
     NAME = "CorrCostStem3D"
 
     def __init__(self, max_disp: int = 48, num_groups: int = 1, act: int = 0):
@@ -207,7 +210,8 @@ class CorrCostStem3DPlugin(_PluginBase):
         out = _Desc()
         if lib().ww_plugin_corr_cost_stem3d_output_dims(self.max_disp, self.num_groups, len(inputs),
                                                         _descs(inputs), ctypes.byref(out)) != 0:
-            raise ValueError("CorrCostStem3D takes left, right [B,C,H,W], w [Cout,G,3,3,3], b [Cout]")
+            raise ValueError("CorrCostStem3D takes left, right [B,C,H,W], w [Cout,G,3,3,3], b [Cout] "
+                             "(or left, right and the six 3-stage weights)")
         return [TensorDesc._from_c(out).dims]
 
     def supports_format_combination(self, pos: int, in_out, nb_inputs: int, nb_outputs: int) -> bool:

@@ -12,7 +12,9 @@
 //
 // B200 design.  The op is HBM-bound: it reads L and R once and writes G*D
 // output values per input pixel per group.  One CTA owns one image row
-// segment of 128 columns for one (b, g) and a band of DT disparities:
+// segment of 128 columns (64 or 32 when the image is that narrow) for one
+// (b, g) and a band of DT disparities (fewer when the grid would not fill
+// the SMs twice):
 //   * the group's L row segment [w0, w0+128) and the matching R segment
 //     [w0 - d0 - DT, w0 - d0 + 128) are staged channel-chunk by chunk into
 //     shared memory with 16-byte vector loads (zero fill off the image, which
@@ -31,10 +33,10 @@
 namespace ww {
 namespace {
 
-constexpr int kTileW = 128;     // columns per CTA (32 threads x 4)
+constexpr int kTileW = 128;     // widest column tile per CTA (32 threads x 4); 64 and 32 for narrow images
 constexpr int kVecW = 4;        // columns per thread
 constexpr int kDispPerThread = 8;
-constexpr int kChunkC = 16;     // channels staged per pass
+constexpr int kChunkC = 16;     // channels staged per pass (32 with the narrow tiles)
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -51,11 +53,56 @@ template <>
 __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 
 // Stage rows [c0, c0+nc) x columns [col0, col0+width) of one (b, h) image row
-// into smem[nc][width], zero outside [0, W).
-template <typename T>
-__device__ __forceinline__ void stage_rows(T* __restrict__ dst, const T* __restrict__ src_row0,
+// into smem[nc][width], zero outside [0, W).  Each thread issues its loads in
+// batches of NB 16-byte vectors before storing any of them, so a chunk costs
+// one memory latency per batch rather than one per vector (the narrow tiles,
+// whose few threads stage ~13 vectors per chunk).
+template <typename T, int NB>
+__device__ __forceinline__ void stage_rows_batched(T* __restrict__ dst, const T* __restrict__ src_row0,
                                            int64_t chan_stride, int nc, int col0, int width, int W,
                                            bool vec_ok)
+{
+    constexpr int kVec = 16 / sizeof(T);
+    const int nvec = width / kVec;  // width is a multiple of kVec
+    const int nthr = blockDim.x * blockDim.y;
+    const int t = threadIdx.y * blockDim.x + threadIdx.x;
+    for (int base = 0; base < nc * nvec; base += NB * nthr) {
+        uint4 v[NB];
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+            const int i = base + k * nthr + t;
+            v[k] = make_uint4(0u, 0u, 0u, 0u);  // zero in both fp16 and fp32
+            if (i < nc * nvec) {
+                const int c = i / nvec;
+                const int gx = col0 + (i - c * nvec) * kVec;
+                const T* src = src_row0 + c * chan_stride;
+                if (vec_ok && gx >= 0 && gx + kVec <= W) {
+                    v[k] = __ldg(reinterpret_cast<const uint4*>(src + gx));
+                } else {
+                    T e[kVec];
+#pragma unroll
+                    for (int q = 0; q < kVec; ++q) {
+                        const int g = gx + q;
+                        e[q] = (g >= 0 && g < W) ? src[g] : from_f32<T>(0.0f);
+                    }
+                    v[k] = *reinterpret_cast<const uint4*>(e);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+            const int i = base + k * nthr + t;
+            if (i < nc * nvec) *reinterpret_cast<uint4*>(dst + i * kVec) = v[k];
+        }
+    }
+}
+
+// The same with one vector per loop trip (the 128-column tiles: measured
+// faster there than the batched form, whose registers cost occupancy).
+template <typename T>
+__device__ __forceinline__ void stage_rows_loop(T* __restrict__ dst, const T* __restrict__ src_row0,
+                                                int64_t chan_stride, int nc, int col0, int width, int W,
+                                                bool vec_ok)
 {
     constexpr int kVec = 16 / sizeof(T);
     const int nvec = width / kVec;  // width is a multiple of kVec
@@ -77,19 +124,28 @@ __device__ __forceinline__ void stage_rows(T* __restrict__ dst, const T* __restr
     }
 }
 
-template <typename T>
+template <typename T, int TW>
+__device__ __forceinline__ void stage_rows(T* __restrict__ dst, const T* __restrict__ src_row0,
+                                           int64_t chan_stride, int nc, int col0, int width, int W,
+                                           bool vec_ok)
+{
+    if constexpr (TW == kTileW) stage_rows_loop<T>(dst, src_row0, chan_stride, nc, col0, width, W, vec_ok);
+    else stage_rows_batched<T, 8>(dst, src_row0, chan_stride, nc, col0, width, W, vec_ok);
+}
+
+template <typename T, int TW, int CC>
 __global__ void __launch_bounds__(256) corr_volume_kernel(
     const T* __restrict__ left, const T* __restrict__ right, T* __restrict__ out,
     int C, int H, int W, int D, int G, int n_dband, int scale_div, float inv_cg, int vec_ok)
 {
-    constexpr int ND = kDispPerThread;
+    constexpr int ND = TW == kTileW ? kDispPerThread : kDispPerThread / 2;
     const int DT = ND * blockDim.y;  // disparities per CTA
-    const int RW = kTileW + DT;      // staged R width
+    const int RW = TW + DT;      // staged R width
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* Ls = reinterpret_cast<T*>(smem_raw);
-    T* Rs = Ls + kChunkC * kTileW;
+    T* Rs = Ls + CC * TW;
 
-    const int w0 = blockIdx.x * kTileW;
+    const int w0 = blockIdx.x * TW;
     const int h = blockIdx.y / n_dband;
     const int d0 = (blockIdx.y - h * n_dband) * DT;
     const int b = blockIdx.z / G;
@@ -111,13 +167,13 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
 #pragma unroll
         for (int v = 0; v < kVecW; ++v) acc[i][v] = 0.0f;
 
-    for (int c0 = 0; c0 < Cg; c0 += kChunkC) {
-        const int nc = min(kChunkC, Cg - c0);
-        stage_rows<T>(Ls, lrow + c0 * plane, plane, nc, w0, kTileW, W, vec_ok);
-        stage_rows<T>(Rs, rrow + c0 * plane, plane, nc, w0 - d0 - DT, RW, W, vec_ok);
+    for (int c0 = 0; c0 < Cg; c0 += CC) {
+        const int nc = min(CC, Cg - c0);
+        stage_rows<T, TW>(Ls, lrow + c0 * plane, plane, nc, w0, TW, W, vec_ok);
+        stage_rows<T, TW>(Rs, rrow + c0 * plane, plane, nc, w0 - d0 - DT, RW, W, vec_ok);
         __syncthreads();
         for (int c = 0; c < nc; ++c) {
-            const T* lp = Ls + c * kTileW + wl;
+            const T* lp = Ls + c * TW + wl;
             const T* rp = Rs + c * RW + rbase;
             float lv[kVecW], rv[ND + kVecW - 1];
 #pragma unroll
@@ -228,26 +284,37 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
     const int scale_div = corr_scale_div_grouped(is_half, B, C, G, H, W, D, dev.sm_count);
     const float inv_cg = 1.0f / static_cast<float>(Cg);
 
-    const int ny = min(8, (D + kDispPerThread - 1) / kDispPerThread);
-    const int DT = ny * kDispPerThread;
+    // Tile shape: the narrowest column tile that covers a row (64 or 32 columns
+    // = 16 or 8 threads across, 32-channel chunks) when the image is narrow:
+    // the reference's native 32 x 40 would otherwise stage and compute three
+    // times the columns it has.
+    const int tw = W <= 32 ? 32 : (W <= 64 ? 64 : kTileW);
+    // Narrow tiles keep 4 disparities per thread (twice the threads of the
+    // 8 the wide tile keeps): a small image has few outputs, and the threads
+    // are what hides the latency of its short fma chains.
+    const int nd = tw == kTileW ? kDispPerThread : kDispPerThread / 2;
+    int ny = min(tw == kTileW ? 8 : 16, (D + nd - 1) / nd);
+    if (tw != kTileW) ny += ny & 1;  // DT a multiple of 8: the staged rows are 16-byte vectors
+    const int DT = ny * nd;
     const int n_dband = (D + DT - 1) / DT;
     if (static_cast<long long>(H) * n_dband > 65535) return WW_ERR_UNSUPPORTED;
-    dim3 block(32, ny);
-    dim3 grid((W + kTileW - 1) / kTileW, H * n_dband, B * G);
+    dim3 block(tw / kVecW, ny);
+    dim3 grid((W + tw - 1) / tw, H * n_dband, B * G);
     const size_t esize = is_half ? 2 : 4;
-    const size_t smem = static_cast<size_t>(kChunkC) * (kTileW + kTileW + DT) * esize;
+    const int cc = tw == kTileW ? kChunkC : 2 * kChunkC;
+    const size_t smem = static_cast<size_t>(cc) * (tw + tw + DT) * esize;
     const int vec_elems = is_half ? 8 : 4;
     const int vec_ok = (W % vec_elems == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(right) % 16 == 0);
-    if (is_half) {
-        corr_volume_kernel<__half><<<grid, block, smem, stream>>>(
-            static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out),
-            C, H, W, D, G, n_dband, scale_div, inv_cg, vec_ok);
-    } else {
-        corr_volume_kernel<float><<<grid, block, smem, stream>>>(
-            static_cast<const float*>(left), static_cast<const float*>(right), static_cast<float*>(out),
-            C, H, W, D, G, n_dband, scale_div, inv_cg, vec_ok);
-    }
+    auto launch = [&](auto tag) {
+        using TT = decltype(tag);
+        auto k = tw == 32 ? corr_volume_kernel<TT, 32, 2 * kChunkC>
+                          : (tw == 64 ? corr_volume_kernel<TT, 64, 2 * kChunkC> : corr_volume_kernel<TT, kTileW, kChunkC>);
+        k<<<grid, block, smem, stream>>>(static_cast<const TT*>(left), static_cast<const TT*>(right),
+                                         static_cast<TT*>(out), C, H, W, D, G, n_dband, scale_div, inv_cg, vec_ok);
+    };
+    if (is_half) launch(__half{});
+    else launch(float{});
     return launch_status("ww_corr_volume");
 }
 

@@ -63,7 +63,7 @@ class WWError(RuntimeError):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m whirlwind_trt_plugins_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python whirlwind_trt_plugins_b200/build.py` "
             "(nvcc, sm_100a). There is no CPU fallback.")
     L = ctypes.CDLL(LIB_PATH)
     p, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float

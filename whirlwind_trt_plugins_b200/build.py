@@ -1,6 +1,8 @@
 """Build libww_trt_plugins.so in-tree for sm_100a with nvcc.
 
-    python -m whirlwind_trt_plugins_b200.build [--force] [--trt-include DIR]
+    python whirlwind_trt_plugins_b200/build.py [--force] [--trt-include DIR]
+
+(run by path: importing the package loads the library this script builds)
 
 Each CUDA/C++ source in csrc/ compiles to an object under _build/ (parallel),
 then everything links into whirlwind_trt_plugins_b200/libww_trt_plugins.so

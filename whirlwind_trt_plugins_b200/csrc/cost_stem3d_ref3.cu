@@ -98,26 +98,32 @@ struct Ref3Params {
     int C, D, H, W, n_dtiles;
     int scale_div;        // correlation scale rule: 1 acc / C, 0 acc * (1 / C)
     float inv_c;
+    int vec_ok;           // W % 8 == 0 and 16-byte aligned features: vector segment loads
 };
 
-// Correlation staging (CORR = true): per chunk of kCorrC channels the left
-// rows [c][14 rows][14 cols] and the right rows [c][14 rows][23 cols] of the
-// brick, fp16, in the space of the two intermediate bricks (free until
-// stage 0).  A thread issues all kStageIt of its loads of a chunk before it
-// stores any (one memory latency per chunk, not one per load).
+// Correlation staging (CORR = true): per chunk of kCorrC channels, fp16, in
+// the space of the two intermediate bricks (free until stage 0), as 16-byte
+// segments aligned in the image row: the left rows [c][14][24 columns from
+// ow0 - 8] (the brick needs ow0 - 3 .. ow0 + 10) and the right rows
+// [c][14][32 columns from rw0 rounded down to 8] (the brick needs
+// rw0 = ow0 - od0 - 9 .. rw0 + 22, every w - d it holds).  A thread issues
+// all kStageIt of its segment loads of a chunk before it stores any (one
+// memory latency per chunk).
 constexpr int kCorrC = 16;
-constexpr int kLTile = I_H * I_W;        // 196
-constexpr int kRW = I_W + I_D - 1;       // 23 right columns: w - d over the brick
-constexpr int kRTile = I_H * kRW;        // 322
-constexpr int kStageIt = (kCorrC * (kLTile + kRTile) + kThreads - 1) / kThreads;
-static_assert(kCorrC * (kLTile + kRTile) * 2 <= (4 * A_VOL + 4 * B_VOL) * 4,
-              "correlation tiles exceed the brick space");
+constexpr int kLW = 24, kRWs = 32;            // staged columns per row
+constexpr int kLSeg = I_H * kLW / 8;          // 42 segments per channel
+constexpr int kRSeg = I_H * kRWs / 8;         // 56
+constexpr int kSegC = kLSeg + kRSeg;          // 98
+constexpr int kStageIt = (kCorrC * kSegC + kThreads - 1) / kThreads;
+constexpr int kLTile = I_H * I_W;             // 196 brick positions (y, x)
+static_assert(kCorrC * kSegC * 16 <= (4 * A_VOL + 4 * B_VOL) * 4, "correlation tiles exceed the brick space");
+static_assert(I_W + 5 <= kLW && I_W + I_D - 1 + 7 <= kRWs, "staged rows too narrow for the brick");
 
 template <bool CORR>
 __global__ void __launch_bounds__(kThreads, CORR ? 2 : 4) cost_stem3d_ref3_kernel(const Ref3Params p)
 {
     __shared__ float s_in[I_VOL];
-    __shared__ float s_ab[4 * A_VOL + 4 * B_VOL];
+    __shared__ __align__(16) float s_ab[4 * A_VOL + 4 * B_VOL];
     __shared__ float4 s_w0q[27];       // [tap] -> 4 output channels
     __shared__ float4 s_w1q[4 * 27];   // [ci][tap] -> 4 output channels
     __shared__ float s_w2[108];        // [ci][tap]
@@ -199,9 +205,12 @@ __global__ void __launch_bounds__(kThreads, CORR ? 2 : 4) cost_stem3d_ref3_kerne
         // +0 where w - d < 0.  Thread (y, x) < (14, 14) owns the brick's 10
         // disparities at that position: one left value and 10 right values
         // (a contiguous run of the right row) per channel.
-        __half* Lt = reinterpret_cast<__half*>(s_ab);  // [kCorrC][14][14]
-        __half* Rt = Lt + kCorrC * kLTile;             // [kCorrC][14][23]
-        const int rw0 = ow0 - od0 - 9;         // image column of right-tile column 0
+        __half* Lt = reinterpret_cast<__half*>(s_ab);  // [kCorrC][14][24]
+        __half* Rt = Lt + kCorrC * I_H * kLW;          // [kCorrC][14][32]
+        const int lw0 = ow0 - 8;                       // ow0 is a multiple of 8
+        const int rw0 = ow0 - od0 - 9;                 // image column of w - d for (x, z) = (0, 9)
+        const int rwa = rw0 & ~7;                      // floor to a multiple of 8
+        const int ro = rw0 - rwa;                      // 0..7
         const int64_t plane = i64(H) * W;
         const __half* lsrc = p.left + i64(b) * p.C * plane;
         const __half* rsrc = p.right + i64(b) * p.C * plane;
@@ -211,36 +220,50 @@ __global__ void __launch_bounds__(kThreads, CORR ? 2 : 4) cost_stem3d_ref3_kerne
         for (int z = 0; z < I_D; ++z) acc[z] = 0.0f;
         for (int c0 = 0; c0 < p.C; c0 += kCorrC) {
             const int nc = min(kCorrC, p.C - c0);
-            const int n_l = nc * kLTile, n_all = nc * (kLTile + kRTile);
-            __half v[kStageIt];
+            uint4 v[kStageIt];
 #pragma unroll
             for (int k = 0; k < kStageIt; ++k) {
                 const int i = tid + k * kThreads;
-                v[k] = __float2half_rn(0.0f);
-                if (i < n_l) {
-                    const int c = i / kLTile, r = i - c * kLTile, yy = r / I_W, xx = r - yy * I_W;
-                    const int gh = oh0 - 3 + yy, gw = ow0 - 3 + xx;
-                    if (gh >= 0 && gh < H && gw >= 0 && gw < W) v[k] = lsrc[i64(c0 + c) * plane + i64(gh) * W + gw];
-                } else if (i < n_all) {
-                    const int q = i - n_l;
-                    const int c = q / kRTile, r = q - c * kRTile, yy = r / kRW, xx = r - yy * kRW;
-                    const int gh = oh0 - 3 + yy, gw = rw0 + xx;
-                    if (gh >= 0 && gh < H && gw >= 0 && gw < W) v[k] = rsrc[i64(c0 + c) * plane + i64(gh) * W + gw];
+                v[k] = make_uint4(0u, 0u, 0u, 0u);
+                if (i < nc * kSegC) {
+                    const int c = i / kSegC, r = i - c * kSegC;
+                    const bool is_l = r < kLSeg;
+                    const int rr = is_l ? r : r - kLSeg;
+                    const int per_row = is_l ? kLW / 8 : kRWs / 8;
+                    const int yy = rr / per_row, seg = rr - yy * per_row;
+                    const int gh = oh0 - 3 + yy, gx = (is_l ? lw0 : rwa) + 8 * seg;
+                    if (gh >= 0 && gh < H) {
+                        const __half* src = (is_l ? lsrc : rsrc) + i64(c0 + c) * plane + i64(gh) * W;
+                        if (p.vec_ok && gx >= 0 && gx + 8 <= W) {
+                            v[k] = __ldg(reinterpret_cast<const uint4*>(src + gx));
+                        } else {
+                            __half e[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const int g = gx + q;
+                                e[q] = (g >= 0 && g < W) ? src[g] : __float2half_rn(0.0f);
+                            }
+                            v[k] = *reinterpret_cast<const uint4*>(e);
+                        }
+                    }
                 }
             }
             __syncthreads();  // the previous chunk's tiles are consumed
 #pragma unroll
             for (int k = 0; k < kStageIt; ++k) {
                 const int i = tid + k * kThreads;
-                if (i < n_l) Lt[i] = v[k];
-                else if (i < n_all) Rt[i - n_l] = v[k];
+                if (i < nc * kSegC) {
+                    const int c = i / kSegC, r = i - c * kSegC;
+                    __half* dst = r < kLSeg ? Lt + c * (I_H * kLW) + r * 8 : Rt + c * (I_H * kRWs) + (r - kLSeg) * 8;
+                    *reinterpret_cast<uint4*>(dst) = v[k];
+                }
             }
             __syncthreads();
             if (tid < kLTile) {
                 for (int c = 0; c < nc; ++c) {
-                    const float lv = __half2float(Lt[c * kLTile + tid]);
-                    // right column of disparity z: (x - z) + 9
-                    const __half* rrow = Rt + c * kRTile + y * kRW + x;
+                    const float lv = __half2float(Lt[c * (I_H * kLW) + y * kLW + x + 5]);
+                    // right column of disparity z: w - d = rw0 + (x - z) + 9
+                    const __half* rrow = Rt + c * (I_H * kRWs) + y * kRWs + ro + x;
 #pragma unroll
                     for (int z = 0; z < I_D; ++z) acc[z] = __fmaf_rn(lv, __half2float(rrow[9 - z]), acc[z]);
                 }
@@ -419,6 +442,8 @@ int corr_cost_stem3d_ref3_launch(const void* left, const void* right, void* out,
     p.left = static_cast<const __half*>(left);
     p.right = static_cast<const __half*>(right);
     p.C = C;
+    p.vec_ok = W % 8 == 0 && reinterpret_cast<uintptr_t>(left) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(right) % 16 == 0;
     return ref3_launch(true, p, B, stream, "ww_corr_cost_stem3d_ref3");
 }
 

@@ -52,7 +52,7 @@ UNIT = "voxels/s"
 # Config 2: dram__bytes_read.sum 25.78 MB + dram__bytes_write.sum 6.37 MB
 # (profiles/stem_tc_fused_c2_full.md; most of the output is still in L2 when
 # the launch ends, so traffic is below the 83.6 MB of algorithmic bytes).
-NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.14e6}
+NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.68e6}
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per step).
 N_E2E_STREAMS = 3
@@ -315,6 +315,9 @@ def bench_nv12(args):
 # Disparity regression workload: the aggregated cost of the batched config
 # (config 4: B = 64, D = 48, 94 x 312), fp16 in and out, soft-argmin.
 DISP_B, DISP_D, DISP_H, DISP_W = 64, 48, 94, 312
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this workload
+# (profiles/disparity_regression_c4_soft_argmin.md)
+DISP_NCU_TRAFFIC_BYTES = 188.2e6
 
 
 def bench_disparity(args):
@@ -411,7 +414,7 @@ def bench_disparity(args):
         "config": {"workload": f"disparity_regression soft-argmin: cost [{B}, {D}, {H}, {W}] fp16 -> [{B}, 1, {H}, {W}]",
                    "l2": f"{n_sets} rotating sets of {in_bytes / 1e6:.0f} MB > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["src"]},
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": DISP_NCU_TRAFFIC_BYTES, "peak_source": peaks["src"]},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)

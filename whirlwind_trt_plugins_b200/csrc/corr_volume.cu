@@ -37,6 +37,7 @@ constexpr int kTileW = 128;     // widest column tile per CTA (32 threads x 4); 
 constexpr int kVecW = 4;        // columns per thread
 constexpr int kDispPerThread = 8;
 constexpr int kChunkC = 16;     // channels staged per pass (32 with the narrow tiles)
+constexpr int kSmallOutputsPerSM = 800;  // below this many outputs per SM: one thread per output
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -216,6 +217,48 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
     }
 }
 
+// Small volumes (fewer than kSmallOutputsPerSM outputs per SM; the
+// reference's native 1 x 48 x 32 x 40 is one): one thread per output, both
+// operands read straight through L2, the channel loop unrolled so 8 channels'
+// loads are in flight at once.  The tiled kernel gives such a volume a few
+// dozen CTAs whose staging round trips and 2048-fma chains are latency the SMs
+// cannot hide.  Same fp32 fma chain in channel order from +0, same scale rule
+// and fp16 rounding, so the result is bit-identical to the tiled kernel's.
+// Output index = ((((b G + g) D + d) H + h) W + w), the [B, G, D, H, W] layout.
+template <typename T>
+__global__ void __launch_bounds__(256) corr_volume_small_kernel(
+    const T* __restrict__ left, const T* __restrict__ right, T* __restrict__ out,
+    int C, int H, int W, int D, int G, int64_t total, int scale_div, float inv_cg)
+{
+    // total < sm_count * kSmallOutputsPerSM: 32-bit index arithmetic (64-bit
+    // division is emulated and would cost more than the dot product).
+    const int i = static_cast<int>(blockIdx.x) * 256 + static_cast<int>(threadIdx.x);
+    if (i >= total) return;
+    int r = i;
+    const int w = r % W;
+    r /= W;
+    const int h = r % H;
+    r /= H;
+    const int d = r % D;
+    r /= D;
+    const int g = r % G;
+    const int b = r / G;
+    const int Cg = C / G;
+    float val = 0.0f;  // w - d < 0: exact +0
+    if (w >= d) {
+        const int64_t plane = i64(H) * W;
+        const int64_t base = (i64(b) * C + i64(g) * Cg) * plane + i64(h) * W;
+        const T* lp = left + base + w;
+        const T* rp = right + base + (w - d);
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int c = 0; c < Cg; ++c, lp += plane, rp += plane)
+            acc = __fmaf_rn(to_f32<T>(__ldg(lp)), to_f32<T>(__ldg(rp)), acc);
+        val = scale_div ? __fdiv_rn(acc, static_cast<float>(Cg)) : __fmul_rn(acc, inv_cg);
+    }
+    out[i] = from_f32<T>(val);
+}
+
 }  // namespace
 
 // Scale rule of the reference kernel that launchCorrVolume<T> would run for a
@@ -283,6 +326,20 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
     const int Cg = C / G;
     const int scale_div = corr_scale_div_grouped(is_half, B, C, G, H, W, D, dev.sm_count);
     const float inv_cg = 1.0f / static_cast<float>(Cg);
+
+    const int64_t total = static_cast<int64_t>(B) * G * D * H * W;
+    if (total < static_cast<int64_t>(dev.sm_count) * kSmallOutputsPerSM) {
+        const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+        if (is_half)
+            corr_volume_small_kernel<__half><<<blocks, 256, 0, stream>>>(
+                static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out),
+                C, H, W, D, G, total, scale_div, inv_cg);
+        else
+            corr_volume_small_kernel<float><<<blocks, 256, 0, stream>>>(
+                static_cast<const float*>(left), static_cast<const float*>(right), static_cast<float*>(out),
+                C, H, W, D, G, total, scale_div, inv_cg);
+        return launch_status("ww_corr_volume");
+    }
 
     // Tile shape: the narrowest column tile that covers a row (64 or 32 columns
     // = 16 or 8 threads across, 32-channel chunks) when the image is narrow:

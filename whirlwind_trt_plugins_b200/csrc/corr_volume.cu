@@ -25,6 +25,9 @@
 //     stores per disparity row.
 // Grid: x = column tiles (fastest, so neighbouring tiles share R in L2),
 // y = row x disparity band, z = batch x group.
+// Volumes too small to fill the SMs with such tiles (the reference's native
+// 1 x 48 x 32 x 40 among them) run corr_volume_small_kernel instead: one
+// thread per output, operands through L2.
 
 #include "ww_common.cuh"
 

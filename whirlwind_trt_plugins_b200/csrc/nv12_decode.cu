@@ -15,7 +15,9 @@
 //
 // B200 shape: the op moves 1.5 bytes in per input pixel and 6 (fp16) or 12
 // (fp32) bytes out per output pixel; nothing is reused beyond the 2x2 taps,
-// which neighbouring outputs share through the read-only cache.  One thread
+// which neighbouring outputs share through the read-only cache; a chroma tap
+// is one 2-byte load of its (U, V) pair (8 loads per output pixel rather than
+// 12: the launch is bound by load latency and issue, not bandwidth).  One thread
 // makes two horizontally adjacent output pixels, so a warp writes 128-byte
 // (fp16) or 256-byte (fp32) contiguous runs of each colour plane with one
 // vector store per lane.  Grid (ceil(W_OUT / 64), ceil(H_OUT / 8), B) of
@@ -51,12 +53,45 @@ __device__ __forceinline__ float bilinear(const uint8_t* __restrict__ plane, int
     return __fmaf_rn(wy0, top, __fmul_rn(wy1, bot));
 }
 
+// Both chroma channels of one tap position at once: U and V are adjacent
+// bytes, so each of the four taps is one 2-byte load, and the weights and
+// clamped indices are computed once.  Per channel the arithmetic is that of
+// bilinear(plane, rows, cols, stride, 2, yf, xf) (and of it at plane + 1).
+__device__ __forceinline__ void bilinear_uv(const uint8_t* __restrict__ chroma, int rows, int cols, int stride,
+                                            float yf, float xf, float& u, float& v)
+{
+    const float fy = floorf(yf), fx = floorf(xf);
+    const int y0 = static_cast<int>(fy), x0 = static_cast<int>(fx);
+    const float wy1 = __fsub_rn(yf, fy), wy0 = __fsub_rn(1.0f, wy1);
+    const float wx1 = __fsub_rn(xf, fx), wx0 = __fsub_rn(1.0f, wx1);
+    const int y0c = clampi(y0, 0, rows - 1), y1c = clampi(y0 + 1, 0, rows - 1);
+    const int x0c = clampi(x0, 0, cols - 1) * 2, x1c = clampi(x0 + 1, 0, cols - 1) * 2;
+    const uint8_t* r0 = chroma + static_cast<int64_t>(y0c) * stride;
+    const uint8_t* r1 = chroma + static_cast<int64_t>(y1c) * stride;
+    // even byte offsets from an even base (the chroma plane starts at
+    // H_IN * W_IN and W_IN is even): 2-byte aligned; low byte U, high byte V
+    const unsigned short t00 = __ldg(reinterpret_cast<const unsigned short*>(r0 + x0c));
+    const unsigned short t01 = __ldg(reinterpret_cast<const unsigned short*>(r0 + x1c));
+    const unsigned short t10 = __ldg(reinterpret_cast<const unsigned short*>(r1 + x0c));
+    const unsigned short t11 = __ldg(reinterpret_cast<const unsigned short*>(r1 + x1c));
+    auto lerp = [&](int sh) {
+        const float v00 = static_cast<float>((t00 >> sh) & 0xff), v01 = static_cast<float>((t01 >> sh) & 0xff);
+        const float v10 = static_cast<float>((t10 >> sh) & 0xff), v11 = static_cast<float>((t11 >> sh) & 0xff);
+        const float top = __fmaf_rn(wx0, v00, __fmul_rn(wx1, v01));
+        const float bot = __fmaf_rn(wx0, v10, __fmul_rn(wx1, v11));
+        return __fmaf_rn(wy0, top, __fmul_rn(wy1, bot));
+    };
+    u = lerp(0);
+    v = lerp(8);
+}
+
 struct Nv12Params {
     const uint8_t* nv12;
     void* out;
     int H_IN, W_IN, H_OUT, W_OUT;
     float sy_h, sy_w, suv_h, suv_w;
-    int vec;  // 1: W_OUT even and the output 8-byte aligned (paired stores)
+    int vec;       // 1: W_OUT even and the output 8-byte aligned (paired stores)
+    int uv_pairs;  // 1: W_IN even and the input 2-byte aligned (one load per chroma tap)
 };
 
 template <bool F16>
@@ -81,8 +116,13 @@ __global__ void __launch_bounds__(kBx * kBy) nv12_decode_kernel(const Nv12Params
         const float xf_y = __fmaf_rn(xo, p.sy_w, -0.5f);
         const float xf_uv = __fmaf_rn(xo, p.suv_w, -0.5f);
         const float Y = bilinear(img, p.H_IN, p.W_IN, p.W_IN, 1, yf_y, xf_y);
-        const float U = bilinear(chroma, H_UV, W_UV, p.W_IN, 2, yf_uv, xf_uv);
-        const float V = bilinear(chroma + 1, H_UV, W_UV, p.W_IN, 2, yf_uv, xf_uv);
+        float U, V;
+        if (p.uv_pairs) {
+            bilinear_uv(chroma, H_UV, W_UV, p.W_IN, yf_uv, xf_uv, U, V);
+        } else {
+            U = bilinear(chroma, H_UV, W_UV, p.W_IN, 2, yf_uv, xf_uv);
+            V = bilinear(chroma + 1, H_UV, W_UV, p.W_IN, 2, yf_uv, xf_uv);
+        }
         const float Cb = __fsub_rn(U, 128.0f), Cr = __fsub_rn(V, 128.0f);
         rgb[0][j] = __fmaf_rn(s, __fmaf_rn(1.402f, Cr, Y), -1.0f);
         rgb[1][j] = __fmaf_rn(s, __fmaf_rn(-0.714136f, Cr, __fmaf_rn(-0.344136f, Cb, Y)), -1.0f);
@@ -140,6 +180,7 @@ int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, 
     p.suv_h = static_cast<float>(H_IN >> 1) / static_cast<float>(H_OUT);
     p.suv_w = static_cast<float>(W_IN >> 1) / static_cast<float>(W_OUT);
     p.vec = (W_OUT % 2 == 0) && (reinterpret_cast<uintptr_t>(out) % 8 == 0);
+    p.uv_pairs = (W_IN % 2 == 0) && (reinterpret_cast<uintptr_t>(nv12) % 2 == 0);
     const dim3 grid(gx, gy, B), block(kBx, kBy);
     if (dtype == WW_DTYPE_HALF) nv12_decode_kernel<true><<<grid, block, 0, stream>>>(p);
     else nv12_decode_kernel<false><<<grid, block, 0, stream>>>(p);

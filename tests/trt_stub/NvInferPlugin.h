@@ -1,0 +1,3 @@
+#pragma once
+// Stand-in: see NvInferRuntime.h in this folder.
+#include "NvInferRuntime.h"

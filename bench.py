@@ -47,11 +47,11 @@ sys.path.insert(0, ROOT)
 METRIC = "cost voxels/s (B*D*H*W) corr+3D stem"
 UNIT = "voxels/s"
 
-# DRAM bytes (read + write) per launch of the fused kernel, from the ncu
-# captures summarised in profiles/ (None until captured for that config).
-# Config 2: dram__bytes_read.sum 25.78 MB + dram__bytes_write.sum 6.37 MB
-# (profiles/stem_tc_fused_c2_full.md; most of the output is still in L2 when
-# the launch ends, so traffic is below the 83.6 MB of algorithmic bytes).
+# DRAM bytes (read + write) per launch of the fused kernel, from an ncu
+# capture of the same workload (None until captured for that config).
+# Config 2: dram__bytes_read.sum 25.24 MB + dram__bytes_write.sum 7.45 MB
+# (most of the output is still in L2 when the launch ends, so traffic is
+# below the 83.6 MB of algorithmic bytes).
 NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.68e6}
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per step).
@@ -327,7 +327,7 @@ def bench_nv12(args):
 # (config 4: B = 64, D = 48, 94 x 312), fp16 in and out, soft-argmin.
 DISP_B, DISP_D, DISP_H, DISP_W = 64, 48, 94, 312
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this workload
-# (profiles/disparity_regression_c4_soft_argmin.md)
+# (ncu capture: 180.2 MB read, the cost volume once, + 8.0 MB written)
 DISP_NCU_TRAFFIC_BYTES = 188.2e6
 
 

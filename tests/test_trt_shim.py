@@ -3,7 +3,7 @@ not installed here, so it is checked with `g++ -fsyntax-only -Werror` against
 stand-in declarations of the IPluginV3 interface (tests/trt_stub/), which
 catch a wrong override, a missing method or a type mismatch against the
 interface the shim implements.  Building it for real needs TensorRT's headers
-(INTEGRATION.md)."""
+and libnvinfer (the build script's --trt-include option)."""
 import os
 import shutil
 import subprocess

@@ -58,6 +58,15 @@ def test_output_shapes_types_formats(pl):
     ins = [T((1, 320, 120, 160)), T((1, 320, 120, 160)), T((32, 40, 3, 3, 3)), T((32,))]
     assert fused.get_output_shapes(ins) == [(1, 32, 48, 120, 160)]
     assert fused.get_fields_to_serialize() == {"max_disp": 48, "num_groups": 40, "act": 0}
+    # 8 inputs: CorrVolume (G = 1) fused with the reference's 3-stage stem
+    native = pl.CorrCostStem3DPlugin(48, 1, 0)
+    eight = [T((1, 64, 32, 40)), T((1, 64, 32, 40))] + [T((n,)) for n in (108, 4, 432, 4, 108, 1)]
+    assert native.get_output_shapes(eight) == [(1, 1, 48, 32, 40)]
+    out = T((1, 1, 48, 32, 40))
+    assert all(native.supports_format_combination(i, eight + [out], 8, 1) for i in range(9))
+    assert not native.supports_format_combination(8, eight + [T((1, 1, 48, 32, 40), 0)], 8, 1)
+    with pytest.raises(ValueError):
+        native.get_output_shapes(eight[:5])
 
 
 @pytest.mark.gpu

@@ -138,6 +138,17 @@ def test_kernel_entry_points_validate_arguments(ww):
     assert L.ww_corr_cost_stem3d(fake, fake, fake, fake, fake, 1, 16, 3, 10, 8, 8, 4, 0, None) == 2
     assert L.ww_corr_cost_stem3d(fake, fake, fake, fake, fake, 1, 16, 2, 10, 8, 8, 4, 5, None) == 2
     assert L.ww_cost_stem3d(None, fake, fake, fake, 1, 4, 4, 4, 4, 4, 0, None) == 4
+    # CorrVolume (G = 1) fused with the 3-stage stem: null, negative size, empty batch
+    ws = [fake] * 6
+    assert L.ww_corr_cost_stem3d_ref3(None, fake, fake, *ws, 1, 64, 32, 40, 48, None) == 4
+    assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 1, 64, -1, 40, 48, None) == 2
+    assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 0, 64, 32, 40, 48, None) == 0
+    # disparity regression: null, dtype, mode, D = 0, empty batch
+    assert L.ww_disparity_regression(None, fake, 1, 1, 1, 8, 4, 4, 0, None) == 4
+    assert L.ww_disparity_regression(fake, fake, 2, 1, 1, 8, 4, 4, 0, None) == 3
+    assert L.ww_disparity_regression(fake, fake, 1, 1, 1, 8, 4, 4, 9, None) == 5
+    assert L.ww_disparity_regression(fake, fake, 1, 1, 1, 0, 4, 4, 0, None) == 2
+    assert L.ww_disparity_regression(fake, fake, 1, 1, 0, 8, 4, 4, 0, None) == 0
 
 
 def test_cost_stem3d_plugin_shapes(ww):

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define WW_ABI_VERSION 1
+#define WW_ABI_VERSION 2
 
 typedef enum ww_status {
     WW_SUCCESS = 0,
@@ -235,7 +235,10 @@ int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_
                                            const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out);
 int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* in_out,
                                                int nb_inputs, int nb_outputs);
-int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act,
+/* nb_inputs selects the form: 4 (left, right, w, b) or 8 (left, right, w0,
+ * b0, w1, b1, w2, b2).  Every input must be fp16; input 1 must have input 0's
+ * shape; the weights and biases must have the element counts of their form. */
+int ww_plugin_corr_cost_stem3d_enqueue(int nb_inputs, int max_disp, int num_groups, int act,
                                        const ww_tensor_desc_t* in_desc,
                                        const void* const* inputs, void* const* outputs,
                                        void* stream);
@@ -265,8 +268,14 @@ int ww_plugin_disparity_regression_enqueue(int mode, const ww_tensor_desc_t* in_
                                            void* const* outputs, void* stream);
 
 /* Device error word written by bounded waits inside the tensor-core kernels
- * (0 = none).  Reading it synchronises the current device.  Clearing resets
- * it to 0. */
+ * (0 = none).  There is ONE word per device, shared by every call, stream and
+ * thread that uses the device: the first wait that expires in any launch
+ * records its code there, and the word keeps it (later expiries do not
+ * overwrite it) until ww_clear_device_error() resets it to 0.  So a non-zero
+ * value says that some launch on the device since the last clear gave up a
+ * wait, not which one; a caller that needs to attribute it clears the word,
+ * runs the call alone and reads it after the call has completed.  Reading
+ * synchronises the current device; clearing is a blocking device write. */
 int ww_device_error(int* code);
 int ww_clear_device_error(void);
 

@@ -40,10 +40,13 @@ def build(force: bool = False) -> str:
     return ORACLE_SO
 
 
-def build_ref() -> str | None:
-    """Compile the reference kernels (needs the reference source tree)."""
-    src = os.environ.get("WW_REF_SRC", "/root/reference/src")
-    if not os.path.isdir(src):
+def build_ref(src: str | None = None) -> str | None:
+    """Compile the reference kernels from the reference project's src/
+    directory: `src`, else $WW_REF_SRC.  Without either (or where that tree
+    does not exist, as on the GPU box) the already built library is used if
+    present."""
+    src = src or os.environ.get("WW_REF_SRC")
+    if not src or not os.path.isdir(src):
         return REF_SO if os.path.exists(REF_SO) else None
     subprocess.run(["make", "-C", _HERE, "ref", f"REF_SRC={src}"], check=True, capture_output=True)
     return REF_SO

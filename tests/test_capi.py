@@ -65,7 +65,7 @@ def test_exports_every_declared_symbol(ww):
 
 def test_abi_version_and_status_strings(ww):
     L = ww.lib()
-    assert L.ww_abi_version() == 1
+    assert L.ww_abi_version() == 2
     assert L.ww_status_string(0) == b"success"
     assert L.ww_status_string(2) == b"invalid tensor shape"
     assert L.ww_status_string(99) == b"unknown status"
@@ -143,6 +143,9 @@ def test_kernel_entry_points_validate_arguments(ww):
     assert L.ww_corr_cost_stem3d_ref3(None, fake, fake, *ws, 1, 64, 32, 40, 48, None) == 4
     assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 1, 64, -1, 40, 48, None) == 2
     assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 0, 64, 32, 40, 48, None) == 0
+    # a correlation over no channels is invalid even when the output is empty
+    assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 0, 0, 32, 40, 48, None) == 2
+    assert L.ww_corr_cost_stem3d_ref3(fake, fake, fake, *ws, 1, 0, 32, 40, 48, None) == 2
     # disparity regression: null, dtype, mode, D = 0, empty batch
     assert L.ww_disparity_regression(None, fake, 1, 1, 1, 8, 4, 4, 0, None) == 4
     assert L.ww_disparity_regression(fake, fake, 2, 1, 1, 8, 4, 4, 0, None) == 3
@@ -183,9 +186,52 @@ def test_corr_cost_stem3d_plugin_shapes(ww):
     ptrs = (ctypes.c_void_p * 4)()
     outs = (ctypes.c_void_p * 1)()
     # weight groups must equal num_groups
-    assert L.ww_plugin_corr_cost_stem3d_enqueue(48, 8, 0, ins, ptrs, outs, None) == 1
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(4, 48, 8, 0, ins, ptrs, outs, None) == 1
     ins32 = descs(desc([1, 320, 120, 160], 0), desc([1, 320, 120, 160], 0), desc([32, 40, 3, 3, 3]), desc([32]))
-    assert L.ww_plugin_corr_cost_stem3d_enqueue(48, 40, 0, ins32, ptrs, outs, None) == 1
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(4, 48, 40, 0, ins32, ptrs, outs, None) == 1
+    # right input of another shape, or a bias count that is not Cout
+    bad_r = descs(desc([1, 320, 120, 160]), desc([1, 320, 119, 160]), desc([32, 40, 3, 3, 3]), desc([32]))
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(4, 48, 40, 0, bad_r, ptrs, outs, None) == 1
+    bad_b = descs(desc([1, 320, 120, 160]), desc([1, 320, 120, 160]), desc([32, 40, 3, 3, 3]), desc([16]))
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(4, 48, 40, 0, bad_b, ptrs, outs, None) == 1
+    # the input count, not the rank of input 2, selects the form
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(5, 48, 40, 0, ins, ptrs, outs, None) == 1
+
+
+def _ref3_descs(w_dims):
+    """left, right [1, 64, 32, 40] and the six 3-stage weights with the given shapes."""
+    return descs(desc([1, 64, 32, 40]), desc([1, 64, 32, 40]), *[desc(d) for d in w_dims])
+
+
+def test_corr_cost_stem3d_plugin_eight_inputs_rank5_weights(ww):
+    """The reference declares w0 as [4, 1, 3, 3, 3] (rank 5): with 8 inputs the
+    plugin must take the 3-stage form whatever the weights' rank, and reject
+    weights whose element counts are not 108/4/432/4/108/1."""
+    L = ww.lib()
+    out = Desc()
+    rank5 = [[4, 1, 3, 3, 3], [4], [4, 4, 3, 3, 3], [4], [1, 4, 3, 3, 3], [1]]
+    ins = _ref3_descs(rank5)
+    assert L.ww_plugin_corr_cost_stem3d_output_dims(48, 1, 8, ins, ctypes.byref(out)) == 0
+    assert list(out.dims[:5]) == [1, 1, 48, 32, 40]
+    ptrs = (ctypes.c_void_p * 8)()
+    outs = (ctypes.c_void_p * 1)()
+    # correct counts reach the kernel entry point, which rejects the null pointers (1)
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(8, 48, 1, 0, ins, ptrs, outs, None) == 1
+    # an empty batch with valid counts is a no-op success: the 3-stage entry
+    # point was taken (the generic form would have read w0 as Cout = 4, G = 1)
+    empty = _ref3_descs(rank5)
+    empty[0].dims[0] = 0
+    empty[1].dims[0] = 0
+    fake = (ctypes.c_void_p * 8)(*([0x1000] * 8))
+    fake_out = (ctypes.c_void_p * 1)(0x1000)
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(8, 48, 1, 0, empty, fake, fake_out, None) == 0
+    # a wrong element count in any weight or bias is rejected before any launch
+    for i in range(6):
+        bad = [list(d) for d in rank5]
+        bad[i][0] += 1
+        assert L.ww_plugin_corr_cost_stem3d_enqueue(8, 48, 1, 0, _ref3_descs(bad), fake, fake_out, None) == 1
+    # num_groups > 1 has no 3-stage form
+    assert L.ww_plugin_corr_cost_stem3d_enqueue(8, 48, 2, 0, empty, fake, fake_out, None) == 1
 
 
 def test_fold_bn_matches_oracle(ww, orc):

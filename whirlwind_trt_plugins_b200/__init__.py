@@ -120,6 +120,20 @@ def _dev(t, name: str, dtype=None):
     return t
 
 
+def _out(out, shape, dtype, device, name: str = "out"):
+    """The output tensor of a call: a new one, or the caller's `out` after
+    checking that it is a contiguous CUDA tensor of exactly `shape` and
+    `dtype` (a smaller one would let the kernel write past its end)."""
+    torch = _torch()
+    shape = tuple(int(s) for s in shape)
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    _dev(out, name, dtype)
+    if tuple(out.shape) != shape:
+        raise ValueError(f"{name} must have shape {shape}, got {tuple(out.shape)}")
+    return out
+
+
 def corr_volume(left, right, max_disp: int, num_groups: int = 1, out=None, stream=None):
     """Group-wise correlation volume.
 
@@ -136,9 +150,7 @@ def corr_volume(left, right, max_disp: int, num_groups: int = 1, out=None, strea
         raise TypeError("corr_volume supports fp16 and fp32")
     B, C, H, W = left.shape
     shape = (B, max_disp, H, W) if num_groups == 1 else (B, num_groups, max_disp, H, W)
-    if out is None:
-        out = torch.empty(shape, dtype=left.dtype, device=left.device)
-    _dev(out, "out", left.dtype)
+    out = _out(out, shape, left.dtype, left.device)
     _check("ww_corr_volume", _lib.ww_corr_volume(left.data_ptr(), right.data_ptr(), out.data_ptr(), dt,
                                                  B, C, H, W, max_disp, num_groups, _stream_ptr(stream)))
     return out
@@ -155,9 +167,7 @@ def cost_stem3d_ref3(vol, w0, b0, w1, b1, w2, b2, out=None, stream=None):
     if vol.dim() != 5 or vol.shape[1] != 1:
         raise ValueError("vol must be [B, 1, D, H, W]")
     B, _, D, H, W = vol.shape
-    if out is None:
-        out = torch.empty_like(vol)
-    _dev(out, "out", torch.float16)
+    out = _out(out, vol.shape, torch.float16, vol.device)
     _check("ww_cost_stem3d_ref3", _lib.ww_cost_stem3d_ref3(vol.data_ptr(), out.data_ptr(),
                                                            *[x.data_ptr() for x in ws], B, D, H, W,
                                                            _stream_ptr(stream)))
@@ -178,9 +188,7 @@ def corr_cost_stem3d_ref3(left, right, w0, b0, w1, b1, w2, b2, max_disp: int = 4
         if x.numel() != n:
             raise ValueError("CostStem3D weight/bias has the wrong size")
     B, C, H, W = left.shape
-    if out is None:
-        out = torch.empty((B, 1, max_disp, H, W), dtype=torch.float16, device=left.device)
-    _dev(out, "out", torch.float16)
+    out = _out(out, (B, 1, max_disp, H, W), torch.float16, left.device)
     _check("ww_corr_cost_stem3d_ref3", _lib.ww_corr_cost_stem3d_ref3(
         left.data_ptr(), right.data_ptr(), out.data_ptr(), *[x.data_ptr() for x in ws], B, C, H, W, max_disp,
         _stream_ptr(stream)))
@@ -199,9 +207,7 @@ def cost_stem3d(vol, w, b, act: int = ACT_RELU, out=None, stream=None):
     Cout = b.numel()
     if w.numel() != Cout * Cin * 27:
         raise ValueError("w must be [Cout, Cin, 3, 3, 3]")
-    if out is None:
-        out = torch.empty((B, Cout, D, H, W), dtype=torch.float16, device=vol.device)
-    _dev(out, "out", torch.float16)
+    out = _out(out, (B, Cout, D, H, W), torch.float16, vol.device)
     _check("ww_cost_stem3d", _lib.ww_cost_stem3d(vol.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
                                                  B, Cin, Cout, D, H, W, act, _stream_ptr(stream)))
     return out
@@ -222,9 +228,7 @@ def corr_cost_stem3d(left, right, w, b, max_disp: int, num_groups: int, act: int
     Cout = b.numel()
     if w.numel() != Cout * num_groups * 27:
         raise ValueError("w must be [Cout, num_groups, 3, 3, 3]")
-    if out is None:
-        out = torch.empty((B, Cout, max_disp, H, W), dtype=torch.float16, device=left.device)
-    _dev(out, "out", torch.float16)
+    out = _out(out, (B, Cout, max_disp, H, W), torch.float16, left.device)
     _check("ww_corr_cost_stem3d", _lib.ww_corr_cost_stem3d(
         left.data_ptr(), right.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
         B, C, num_groups, H, W, max_disp, Cout, act, _stream_ptr(stream)))
@@ -239,11 +243,13 @@ def corr_cost_stem3d_band(left_band, right_band, w, b, max_disp: int, num_groups
     torch = _torch()
     for t, n in ((left_band, "left"), (right_band, "right"), (w, "w"), (b, "b")):
         _dev(t, n, torch.float16)
+    if left_band.dim() != 4 or left_band.shape != right_band.shape:
+        raise ValueError("left_band/right_band must both be [B, C, in_rows, W]")
     B, C, in_rows, W = left_band.shape
     Cout = b.numel()
-    if out is None:
-        out = torch.empty((B, Cout, max_disp, out_rows, W), dtype=torch.float16, device=left_band.device)
-    _dev(out, "out", torch.float16)
+    if w.numel() != Cout * num_groups * 27:
+        raise ValueError("w must be [Cout, num_groups, 3, 3, 3]")
+    out = _out(out, (B, Cout, max_disp, out_rows, W), torch.float16, left_band.device)
     _check("ww_corr_cost_stem3d_band", _lib.ww_corr_cost_stem3d_band(
         left_band.data_ptr(), right_band.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
         B, C, num_groups, H, W, max_disp, Cout, act, in_row0, in_rows, out_row0, out_rows,
@@ -271,9 +277,7 @@ def nv12_decode(nv12, out_h: int = 224, out_w: int = 288, dtype=None, out=None, 
     dt = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}.get(dtype)
     if dt is None:
         raise TypeError("output dtype must be float16 or float32")
-    if out is None:
-        out = torch.empty((B, 3, out_h, out_w), dtype=dtype, device=x.device)
-    _dev(out, "out", dtype)
+    out = _out(out, (B, 3, out_h, out_w), dtype, x.device)
     _check("ww_nv12_decode", _lib.ww_nv12_decode(x.data_ptr(), out.data_ptr(), dt, B, H_NV12 * 2 // 3, W_IN,
                                                  out_h, out_w, _stream_ptr(stream)))
     return out
@@ -285,13 +289,10 @@ def disparity_regression(cost, mode: int = DISP_SOFTARGMAX, dtype=None, out=None
     cost is a similarity) or -1 (DISP_SOFTARGMIN, cost is a matching cost);
     fp32 arithmetic, output dtype = input dtype unless `dtype` is given."""
     torch = _torch()
-    if not isinstance(cost, torch.Tensor) or not cost.is_cuda:
-        raise TypeError("cost must be a CUDA tensor")
+    _dev(cost, "cost")
     dts = {torch.float16: DTYPE_HALF, torch.float32: DTYPE_FLOAT}
     if cost.dtype not in dts:
         raise TypeError("cost must be float16 or float32")
-    if not cost.is_contiguous():
-        raise ValueError("cost must be contiguous")
     if cost.dim() == 5 and cost.shape[1] == 1:
         B, _, D, H, W = cost.shape
     elif cost.dim() == 4:
@@ -303,9 +304,7 @@ def disparity_regression(cost, mode: int = DISP_SOFTARGMAX, dtype=None, out=None
     dtype = dtype or cost.dtype
     if dtype not in dts:
         raise TypeError("output dtype must be float16 or float32")
-    if out is None:
-        out = torch.empty((B, 1, H, W), dtype=dtype, device=cost.device)
-    _dev(out, "out", dtype)
+    out = _out(out, (B, 1, H, W), dtype, cost.device)
     _check("ww_disparity_regression", _lib.ww_disparity_regression(
         cost.data_ptr(), out.data_ptr(), dts[cost.dtype], dts[dtype], B, D, H, W, mode, _stream_ptr(stream)))
     return out

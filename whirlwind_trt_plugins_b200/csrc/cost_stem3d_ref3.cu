@@ -387,8 +387,10 @@ int ref3_launch(bool corr, Ref3Params& p, int B, cudaStream_t stream, const char
 {
     if (!p.w0 || !p.b0 || !p.w1 || !p.b1 || !p.w2 || !p.b2 || !p.out) return WW_ERR_NULL_POINTER;
     if (B < 0 || p.D < 0 || p.H < 0 || p.W < 0 || p.C < 0) return WW_ERR_INVALID_SHAPE;
-    if (B == 0 || p.D == 0 || p.H == 0 || p.W == 0) return WW_SUCCESS;
+    // A correlation over no channels is invalid whatever the output size
+    // (as in corr_volume_launch), so C is checked before the empty-output exit.
     if (corr && p.C == 0) return WW_ERR_INVALID_SHAPE;
+    if (B == 0 || p.D == 0 || p.H == 0 || p.W == 0) return WW_SUCCESS;
     p.n_dtiles = (p.D + TD - 1) / TD;
     if (static_cast<long long>(B) * p.n_dtiles > 65535 || (p.H + TH - 1) / TH > 65535) return WW_ERR_UNSUPPORTED;
     DeviceInfo dev;

@@ -17,6 +17,26 @@ bool is_linear_half(const ww_tensor_desc_t& d)
 
 bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffff; }
 
+bool same_shape(const ww_tensor_desc_t& a, const ww_tensor_desc_t& b)
+{
+    if (a.nb_dims != b.nb_dims || a.nb_dims < 0 || a.nb_dims > 8) return false;
+    for (int i = 0; i < a.nb_dims; ++i)
+        if (a.dims[i] != b.dims[i]) return false;
+    return true;
+}
+
+// Element count of a descriptor; -1 for a negative (unknown) or invalid shape.
+int64_t numel(const ww_tensor_desc_t& d)
+{
+    if (d.nb_dims < 0 || d.nb_dims > 8) return -1;
+    int64_t n = 1;
+    for (int i = 0; i < d.nb_dims; ++i) {
+        if (d.dims[i] < 0) return -1;
+        n *= d.dims[i];
+    }
+    return n;
+}
+
 }  // namespace
 
 extern "C" {
@@ -187,19 +207,27 @@ int ww_plugin_corr_cost_stem3d_supports_format(int pos, const ww_tensor_desc_t* 
     return is_linear_half(in_out[pos]);
 }
 
-int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act, const ww_tensor_desc_t* in_desc,
-                                       const void* const* inputs, void* const* outputs, void* stream)
+int ww_plugin_corr_cost_stem3d_enqueue(int nb_inputs, int max_disp, int num_groups, int act,
+                                       const ww_tensor_desc_t* in_desc, const void* const* inputs,
+                                       void* const* outputs, void* stream)
 {
     if (in_desc == nullptr || inputs == nullptr || outputs == nullptr) return 1;
+    if (nb_inputs != 4 && nb_inputs != 8) return 1;
     const ww_tensor_desc_t& d = in_desc[0];
-    if (d.nb_dims != 4) return 1;
+    if (d.nb_dims != 4 || !same_shape(d, in_desc[1])) return 1;
     for (int i = 0; i < 4; ++i)
         if (!fits_int(d.dims[i])) return 1;
-    if (d.dtype != WW_DTYPE_HALF) return 1;
-    if (in_desc[2].nb_dims != 5) {
-        // 8 inputs: CorrVolume (G = 1) fused with the reference's 3-stage
-        // CostStem3D; num_groups must be 1 and act is ReLU6 by definition.
+    for (int i = 0; i < nb_inputs; ++i)
+        if (in_desc[i].dtype != WW_DTYPE_HALF) return 1;
+    if (nb_inputs == 8) {
+        // CorrVolume (G = 1) fused with the reference's 3-stage CostStem3D:
+        // w0 [4,1,3,3,3] b0 [4] w1 [4,4,3,3,3] b1 [4] w2 [1,4,3,3,3] b2 [1]
+        // (cost_stem_3d_kernel.hpp:8-15), any rank with those element
+        // counts; num_groups must be 1 and the activation is ReLU6.
+        static const int64_t kCounts[6] = {108, 4, 432, 4, 108, 1};
         if (num_groups > 1) return 1;
+        for (int i = 0; i < 6; ++i)
+            if (numel(in_desc[2 + i]) != kCounts[i]) return 1;
         const int st = ww_corr_cost_stem3d_ref3(inputs[0], inputs[1], outputs[0], inputs[2], inputs[3], inputs[4],
                                                 inputs[5], inputs[6], inputs[7], static_cast<int>(d.dims[0]),
                                                 static_cast<int>(d.dims[1]), static_cast<int>(d.dims[2]),
@@ -208,8 +236,10 @@ int ww_plugin_corr_cost_stem3d_enqueue(int max_disp, int num_groups, int act, co
     }
     const ww_tensor_desc_t& wd = in_desc[2];
     const int G = num_groups <= 0 ? 1 : num_groups;
-    if (wd.dims[1] != G || wd.dims[2] != 3 || wd.dims[3] != 3 || wd.dims[4] != 3 || !fits_int(wd.dims[0])) return 1;
-    if (d.dtype != WW_DTYPE_HALF) return 1;
+    if (wd.nb_dims != 5 || wd.dims[1] != G || wd.dims[2] != 3 || wd.dims[3] != 3 || wd.dims[4] != 3 ||
+        !fits_int(wd.dims[0]))
+        return 1;
+    if (numel(in_desc[3]) != wd.dims[0]) return 1;  // one bias per output channel
     const int st = ww_corr_cost_stem3d(inputs[0], inputs[1], inputs[2], inputs[3], outputs[0],
                                        static_cast<int>(d.dims[0]), static_cast<int>(d.dims[1]), G,
                                        static_cast<int>(d.dims[2]), static_cast<int>(d.dims[3]), max_disp,

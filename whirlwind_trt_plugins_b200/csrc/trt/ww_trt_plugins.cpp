@@ -253,7 +253,7 @@ public:
             case Op::kCostStem3D:
                 return ww_plugin_cost_stem3d_enqueue(nin, mFields.act, d.data(), inputs, outputs, stream);
             case Op::kCorrCostStem3D:
-                return ww_plugin_corr_cost_stem3d_enqueue(mFields.max_disp, mFields.num_groups, mFields.act,
+                return ww_plugin_corr_cost_stem3d_enqueue(nin, mFields.max_disp, mFields.num_groups, mFields.act,
                                                           d.data(), inputs, outputs, stream);
             case Op::kNv12Decode: {
                 if (outDesc == nullptr) return 1;

@@ -218,7 +218,7 @@ class CorrCostStem3DPlugin(_PluginBase):
         return bool(lib().ww_plugin_corr_cost_stem3d_supports_format(pos, _descs(in_out), nb_inputs, nb_outputs))
 
     def enqueue(self, input_desc, inputs, outputs, stream=None) -> int:
-        return lib().ww_plugin_corr_cost_stem3d_enqueue(self.max_disp, self.num_groups, self.act,
+        return lib().ww_plugin_corr_cost_stem3d_enqueue(len(input_desc), self.max_disp, self.num_groups, self.act,
                                                         _descs(input_desc), _ptrs(inputs), _ptrs(outputs),
                                                         ctypes.c_void_p(_stream(stream)))
 

@@ -1,38 +1,50 @@
 """Benchmark of the fused stereo front end (group-wise correlation -> 3x3x3
 stem) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 4] [--impl ours|reference]
 
-One step = one fused correlation + stem pass (ww_corr_cost_stem3d) over one
-batch of the workload (default: config 2, B=1 C=320 G=40 H=120 W=160 D=48
-Cout=32, fp16).  Under torchrun (N > 1) every rank runs its own batch on its
-own GPU: the path partitions by batch with no exchange, so scaling is weak
-(global batch = N x B) and no collective touches the data path.
+One step = one fused correlation + stem pass (ww_corr_cost_stem3d) over the
+whole batch of the workload.  The headline workload is config 4, the batched
+wide-aspect stereo set (B=64 C=256 G=32 H=94 W=312 D=48 Cout=32, fp16, 5 %
+of the pixels zeroed), the largest configuration that fits one GPU.  Under
+torchrun (N > 1) its 64 pairs are split across the ranks (split_even), each
+rank computing its share on its own GPU with no collective on the data
+path: the global batch is fixed, so scaling is strong.
 
 Printed (rank 0, one JSON line):
-  value      whole-job cost voxels/s (B*D*H*W per step, summed over ranks),
+  value      whole-job cost voxels/s (B*D*H*W of the full batch per step),
              inputs resident in HBM, CUDA-event time of exactly K steps, max
-             over ranks; K steps rotate over input/output sets whose total
-             size exceeds the 126 MB L2, so no step reads another's cache.
-  e2e        the same metric through the public API from pinned HOST buffers:
-             every step copies left/right host->device, runs the op and copies
-             the whole output volume device->host, all inside the timed region;
-             steps rotate over three streams so copies overlap other steps.
+             over ranks.  Every step's inputs (1.9 GB for config 4) are
+             larger than the 126 MB L2; smaller configs rotate over input /
+             output sets of >= 400 MB.
+  e2e        the same metric through the public API from pinned HOST
+             buffers: every step copies its pairs host->device, runs the op
+             and copies the whole output device->host, all inside the timed
+             region (chunks of the batch rotate over three streams so the
+             copies overlap the kernels).
   roofline   the fused kernel against the measured B200 peaks
-             (MEASURED_PEAKS.json): algorithmic stem FLOPs / kernel time vs
-             the bf16/fp16 tensor peak, and algorithmic bytes / time vs HBM.
+             (MEASURED_PEAKS.json): stem FLOPs / kernel time vs the bf16 / fp16
+             tensor peak, algorithmic bytes / time vs HBM; `traffic` from an
+             ncu capture of the same kernel (per launch).
   cpu_baseline  the CPU oracle (plain-C restatement of the reference's
              semantics; the reference has no CPU implementation of its own)
              on a bounded row band of the same workload, all host threads.
---impl reference times that CPU implementation on the same workload
-(rank 0 only; the other ranks exit 0).
+  secondary  the other configurations measured the same way in the same run:
+             at N = 1 configs 2, 3 and 5 (config 5 also as us per call); at
+             N > 1 config 3 split into row bands over the N ranks, the
+             one-row halo exchange (NCCL send/recv) inside the timed region.
+--impl reference times the CPU implementation on the same workload (rank 0
+only; the other ranks exit 0) and loads nothing from the product package.
 
---op nv12_decode measures the camera decode instead (one GPU, NV12_B 720p
-frames -> 224 x 288 fp16; HBM roofline; the C oracle as the CPU baseline).
+Other ops (one GPU): --op nv12_decode (camera decode), --op
+disparity_regression (soft-argmin after aggregation), --op stem3_native (the
+reference's 3-stage stem at its native shape, alone and fused with its G = 1
+correlation).
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -46,31 +58,44 @@ sys.path.insert(0, ROOT)
 
 METRIC = "cost voxels/s (B*D*H*W) corr+3D stem"
 UNIT = "voxels/s"
+DEFAULT_CONFIG = 4
 
-# DRAM bytes (read + write) per launch of the fused kernel, from an ncu
-# capture of the same workload (None until captured for that config).
-# Config 2: dram__bytes_read.sum 25.24 MB + dram__bytes_write.sum 7.45 MB
-# (most of the output is still in L2 when the launch ends, so traffic is
-# below the 83.6 MB of algorithmic bytes).
+# DRAM bytes (read + write) per launch of the fused kernel on the full
+# configuration, from ncu captures (profiles/stem_tc_fused_*.md; None until
+# captured).  Config 2: dram__bytes_read.sum 25.24 MB + dram__bytes_write.sum
+# 7.45 MB (most of the output is still in L2 when the launch ends).
 NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.68e6}
 
-# Streams the end-to-end loop rotates over (copy in, op, copy out per step).
+# Streams the end-to-end loop rotates over (copy in, op, copy out per chunk).
 N_E2E_STREAMS = 3
+
+
+def load_configs():
+    """whirlwind_trt_plugins_b200/configs.py by its path: importing it as part
+    of the package would run the package __init__ and load the CUDA library,
+    which the reference arm must not do."""
+    spec = importlib.util.spec_from_file_location(
+        "ww_bench_configs", os.path.join(ROOT, "whirlwind_trt_plugins_b200", "configs.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=DEFAULT_CONFIG)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the configuration's batch (profiling captures of a smaller case)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode", "disparity_regression"],
-                    default="corr_cost_stem3d",
-                    help="corr_cost_stem3d (the headline), nv12_decode (the camera decode, one GPU) or "
-                         "disparity_regression (soft-argmin after aggregation, one GPU)")
+    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode", "disparity_regression", "stem3_native"],
+                    default="corr_cost_stem3d")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver for ncu: one input set, W + K launches, nothing else")
     return ap.parse_args()
@@ -81,8 +106,28 @@ def load_peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"],
+                "tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def workload_name(cfg) -> str:
+    return (f"{cfg.name}: B={cfg.B} C={cfg.C} G={cfg.G} H={cfg.H} W={cfg.W} D={cfg.D} Cout={cfg.Cout} fp16"
+            + (f", {cfg.zero_frac:.0%} of pixels zeroed" if cfg.zero_frac else ""))
+
+
+def config_dict(cfg, world: int, mode: str = "batch") -> dict:
+    """The workload description both arms print (identical for the same run)."""
+    if mode == "rows":
+        par = f"row bands over {world} GPU(s), one-row halo by NCCL send/recv, no collective in the op"
+    elif world > 1:
+        par = f"batch split over {world} GPUs (split_even), no collective in the op"
+    else:
+        par = "one GPU"
+    per_set = cfg.algorithmic_bytes()
+    l2 = (f"each step's inputs and output ({per_set / 1e9:.1f} GB) exceed the 126 MB L2"
+          if per_set > 400 * 2**20 else "steps rotate over input/output sets totalling >= 400 MB (> 126 MB L2)")
+    return {"workload": workload_name(cfg), "global_batch": cfg.B, "parallelism": par, "l2": l2}
 
 
 class ClockSampler:
@@ -138,10 +183,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample_inputs(cfg, rows: int):
+# ----------------------------------------------------------------- CPU arm
+
+def cpu_sample_inputs(C, cfg, rows: int):
     """Inputs for output rows [0, rows) of batch item 0 (plus the halo row)."""
-    from whirlwind_trt_plugins_b200.configs import make_inputs
-    return make_inputs(cfg.scaled(B=1, H=min(cfg.H, rows + 1)))
+    return C.make_inputs(cfg.scaled(B=1, H=min(cfg.H, rows + 1)))
 
 
 def cpu_oracle_seconds(cfg, x, rows: int, nthreads: int) -> float:
@@ -149,40 +195,41 @@ def cpu_oracle_seconds(cfg, x, rows: int, nthreads: int) -> float:
     rows [0, rows) of batch item 0."""
     import oracle
     t0 = time.perf_counter()
-    oracle.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=oracle.ACC_F32_SEQ,
-                     rows=(0, rows), nthreads=nthreads)
+    oracle.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, act=cfg.act,
+                     acc_mode=oracle.ACC_F32_SEQ, rows=(0, rows), nthreads=nthreads)
     return time.perf_counter() - t0
 
 
-def pick_cpu_rows(cfg, budget_s: float, nthreads: int) -> int:
+def pick_cpu_rows(C, cfg, budget_s: float, nthreads: int) -> int:
     """Rows of batch item 0 whose oracle time is about `budget_s` seconds."""
     probe = min(cfg.H, 4)
-    dt = cpu_oracle_seconds(cfg, cpu_sample_inputs(cfg, probe), probe, nthreads) / probe
+    dt = cpu_oracle_seconds(cfg, cpu_sample_inputs(C, cfg, probe), probe, nthreads) / probe
     return max(1, min(cfg.H, int(budget_s / max(dt, 1e-4))))
 
 
-def cpu_baseline(cfg, budget_s: float = 12.0) -> dict:
+def cpu_baseline(C, cfg, budget_s: float) -> dict:
     import oracle
     n = oracle.nthreads_default()
-    rows = pick_cpu_rows(cfg, budget_s, n)
-    x = cpu_sample_inputs(cfg, rows)
+    rows = pick_cpu_rows(C, cfg, budget_s, n)
+    x = cpu_sample_inputs(C, cfg, rows)
     dt = cpu_oracle_seconds(cfg, x, rows, n)
     return {"value": rows * cfg.W * cfg.D / dt, "unit": UNIT, "cores": n, "kind": "port",
             "sample": f"output rows [0,{rows}) of batch item 0 of {cfg.name}: corr+stem in the C oracle "
                       f"(fp32 accumulation), {dt:.1f} s"}
 
 
-def run_reference(args, cfg, rank):
-    """Reference arm: the CPU implementation of the path (the oracle port),
-    each step a bounded row band of the workload; the whole run is sized to
-    about two minutes."""
+def run_reference(args, C, cfg, rank, world):
+    """Reference arm: the CPU implementation of the path (the oracle port of
+    the reference's semantics), each step a bounded row band of the
+    workload; the whole run is sized to about two minutes.  Nothing from the
+    product package is imported."""
     if rank != 0:
         return
     import oracle
     n = oracle.nthreads_default()
     per_step = min(2.0, 120.0 / max(1, args.steps + args.warmup))
-    rows = pick_cpu_rows(cfg, per_step, n)
-    x = cpu_sample_inputs(cfg, rows)
+    rows = pick_cpu_rows(C, cfg, per_step, n)
+    x = cpu_sample_inputs(C, cfg, rows)
     for _ in range(args.warmup):
         cpu_oracle_seconds(cfg, x, rows, n)
     times = [cpu_oracle_seconds(cfg, x, rows, n) for _ in range(args.steps)]
@@ -190,10 +237,11 @@ def run_reference(args, cfg, rank):
     value = vox * len(times) / sum(times)
     sample = f"output rows [0,{rows}) of batch item 0 of {cfg.name} per step (corr+stem, fp32 accumulation)"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic", "config": {"workload": cfg.name},
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic (seeded normal/uniform features, N(0,0.05) weights)",
+        "config": config_dict(cfg, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": n, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU implementation of this path; its semantics run as the "
@@ -201,6 +249,344 @@ def run_reference(args, cfg, rank):
     }
     print(json.dumps(line), flush=True)
 
+
+# ----------------------------------------------------------------- GPU arm
+
+class Ctx:
+    def __init__(self, world, rank, local):
+        import torch
+        self.world, self.rank, self.local = world, rank, local
+        torch.cuda.set_device(local)
+        self.dev = torch.device("cuda", local)
+        self.dist = None
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], device=self.dev, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def roofline(cfg, ms_per_step: float, peaks: dict) -> dict:
+    """The fused kernel (the only kernel of a step) against the measured peaks."""
+    t = ms_per_step * 1e-3
+    tflops = cfg.stem_flops() / t / 1e12
+    gbs = cfg.algorithmic_bytes() / t / 1e9
+    f_tc, f_hbm = tflops / peaks["tflops"], gbs / peaks["hbm_gbs"]
+    if f_tc >= f_hbm:
+        roof = {"bound": "tensor", "achieved": tflops, "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": f_tc}
+    else:
+        roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": f_hbm}
+    roof.update({"traffic": NCU_TRAFFIC_BYTES.get(cfg.name), "peak_source": peaks["src"] + " (burst)",
+                 "other": {"hbm_gbs": gbs, "hbm_frac": f_hbm, "tensor_tflops": tflops, "tensor_frac": f_tc,
+                           "tensor_frac_of_sustained": (tflops / peaks["tflops_sustained"]
+                                                        if peaks.get("tflops_sustained") else None),
+                           "algorithmic_bytes": cfg.algorithmic_bytes(), "stem_flops": cfg.stem_flops()}})
+    return roof
+
+
+def local_batch(cfg, ctx) -> tuple[int, int]:
+    from whirlwind_trt_plugins_b200.shard import split_even
+    return split_even(cfg.B, ctx.world, ctx.rank)
+
+
+def make_sets(C, cfg, ctx, b_local: int, n_max: int):
+    """Rotating resident input/output sets of this rank's share of the batch."""
+    import torch
+    lcfg = cfg.scaled(B=b_local)
+    per_set = lcfg.algorithmic_bytes()
+    n_sets = min(n_max, max(1, -(-400 * 2**20 // max(per_set, 1))))
+    sets = []
+    for s in range(n_sets):
+        x = C.make_inputs_torch(lcfg, ctx.dev, seed=1000 * ctx.rank + 10 * s)
+        out = torch.empty((b_local, cfg.Cout, cfg.D, cfg.H, cfg.W), dtype=torch.float16, device=ctx.dev)
+        sets.append((x["left"], x["right"], x["w"], x["b"], out))
+    return sets
+
+
+def time_steps(ctx, step, steps: int, soak_s: float, clocks: bool):
+    """CUDA-event time (ms) of exactly `steps` steps after a soak, max over
+    ranks; nvidia-smi clocks sampled during the soak and the timed region."""
+    import torch
+    stream = torch.cuda.current_stream()
+    sampler = ClockSampler(ctx.local) if clocks else None
+    if sampler is not None:
+        sampler.__enter__()
+    try:
+        t_end = time.time() + soak_s
+        i = 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+            if i % 16 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        ctx.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.barrier()
+    finally:
+        if sampler is not None:
+            sampler.__exit__()
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    return ms, (sampler.summary() if sampler is not None else None)
+
+
+def e2e_batch(ww, cfg, ctx, src, b_local: int, steps: int) -> dict | None:
+    """End to end through the public API from pinned host memory: per step
+    this rank's pairs go host->device, through ww.corr_cost_stem3d and the
+    whole output back device->host, in chunks of the batch rotating over
+    N_E2E_STREAMS streams (each with its own device buffers), so one chunk's
+    copies overlap another's kernel."""
+    import torch
+    if b_local == 0:          # same collective sequence as the ranks with work
+        ctx.barrier()
+        ctx.max_over_ranks(0.0)
+        return None
+    L, R, w, b = src          # resident inputs: copied once into the host buffers
+    chunk = max(1, min(b_local, 4))
+    n_chunks = -(-b_local // chunk)
+    shape_in = (b_local, cfg.C, cfg.H, cfg.W)
+    shape_out = (b_local, cfg.Cout, cfg.D, cfg.H, cfg.W)
+    hL = torch.empty(shape_in, dtype=torch.float16, pin_memory=True)
+    hR = torch.empty(shape_in, dtype=torch.float16, pin_memory=True)
+    hL.copy_(L)
+    hR.copy_(R)
+    del L, R
+    hout = torch.empty(shape_out, dtype=torch.float16, pin_memory=True)
+    lanes = []
+    for _ in range(N_E2E_STREAMS):
+        lanes.append({"s": torch.cuda.Stream(ctx.dev),
+                      "dL": torch.empty((chunk,) + shape_in[1:], dtype=torch.float16, device=ctx.dev),
+                      "dR": torch.empty((chunk,) + shape_in[1:], dtype=torch.float16, device=ctx.dev),
+                      "dout": torch.empty((chunk,) + shape_out[1:], dtype=torch.float16, device=ctx.dev)})
+
+    def run_step():
+        for k in range(n_chunks):
+            ln = lanes[k % N_E2E_STREAMS]
+            c0, c1 = k * chunk, min(b_local, (k + 1) * chunk)
+            n = c1 - c0
+            with torch.cuda.stream(ln["s"]):
+                ln["dL"][:n].copy_(hL[c0:c1], non_blocking=True)
+                ln["dR"][:n].copy_(hR[c0:c1], non_blocking=True)
+                ww.corr_cost_stem3d(ln["dL"][:n], ln["dR"][:n], w, b, cfg.D, cfg.G, act=cfg.act,
+                                    out=ln["dout"][:n], stream=ln["s"])
+                hout[c0:c1].copy_(ln["dout"][:n], non_blocking=True)
+
+    stream = torch.cuda.current_stream()
+    run_step()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for ln in lanes:                      # every lane starts after f0
+        ln["s"].wait_stream(stream)
+    for _ in range(steps):
+        run_step()
+    for ln in lanes:                      # f1 waits for every lane
+        stream.wait_stream(ln["s"])
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = ctx.max_over_ranks(f0.elapsed_time(f1))
+    return {"value": cfg.voxels * steps / (ems * 1e-3), "unit": UNIT,
+            "h2d_bytes_per_step": 2 * hL.numel() * 2, "d2h_bytes_per_step": hout.numel() * 2,
+            "steps": steps, "streams": N_E2E_STREAMS, "chunk_pairs": chunk,
+            "note": "bytes are this rank's share; the value counts the whole batch over the max-over-ranks time"}
+
+
+def bench_config(args, C, ww, cfg, ctx, *, steps, soak_s, clocks, e2e_steps, cpu_budget_s):
+    """Batch-split (or single-GPU) measurement of one configuration."""
+    import torch
+    b0, b1 = local_batch(cfg, ctx)
+    b_local = b1 - b0
+    sets = make_sets(C, cfg, ctx, b_local, n_max=1 if args.profile else 8) if b_local else []
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        if not sets:
+            return
+        L, R, w, b, out = sets[i % len(sets)]
+        ww.corr_cost_stem3d(L, R, w, b, cfg.D, cfg.G, act=cfg.act, out=out, stream=stream)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(steps):
+            step(i)
+        torch.cuda.synchronize()
+        return {"profile": f"{cfg.name} B={b_local}: {max(3, args.warmup)} + {steps} launches of the fused kernel"}
+    ms, clk = time_steps(ctx, step, steps, soak_s, clocks)
+    if ww.device_error() != 0:
+        raise SystemExit("device error word set during the benchmark")
+    ms_per_step = ms / steps
+    res = {"value": cfg.voxels * steps / (ms * 1e-3), "ms_per_step": ms_per_step,
+           "roofline": roofline(cfg.scaled(B=b_local) if ctx.world > 1 else cfg, ms_per_step, load_peaks()),
+           "gpu_launches": steps if b_local else 0, "clocks": clk,
+           "n_sets": len(sets)}
+    if ctx.world > 1:
+        res["roofline"]["note"] = f"per GPU: {b_local} of {cfg.B} pairs on rank {ctx.rank}"
+    src = sets[0][:4] if sets else None
+    del sets
+    if not args.no_e2e:
+        res["e2e"] = e2e_batch(ww, cfg, ctx, src, b_local, e2e_steps)
+    else:
+        res["e2e"] = None
+    del src
+    torch.cuda.empty_cache()
+    res["cpu_baseline"] = None
+    if not args.no_cpu_baseline and ctx.world == 1 and cpu_budget_s > 0:
+        try:
+            res["cpu_baseline"] = cpu_baseline(C, cfg, cpu_budget_s)
+        except Exception as e:  # the baseline never blocks the measurement
+            res["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": None, "kind": "port",
+                                   "sample": f"failed: {e}"}
+    return res
+
+
+def us_per_call(ww, C, cfg, ctx, calls: int = 200) -> dict:
+    """Config 5's latency figures: device time per call from one CUDA graph of
+    `calls` launches, and wall time per call of the Python API issuing them."""
+    import torch
+    x = C.make_inputs_torch(cfg, ctx.dev, seed=77)
+    out = torch.empty((cfg.B, cfg.Cout, cfg.D, cfg.H, cfg.W), dtype=torch.float16, device=ctx.dev)
+
+    def call(s):
+        ww.corr_cost_stem3d(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, act=cfg.act, out=out, stream=s)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(5):
+        call(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap):
+        for _ in range(calls):
+            call(torch.cuda.current_stream())
+    stream.wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dev_us = e0.elapsed_time(e1) * 1e3 / calls
+    del graph
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        call(stream)
+    torch.cuda.synchronize()
+    host_us = (time.perf_counter() - t0) * 1e6 / calls
+    return {"us_per_call": dev_us, "us_per_call_api": host_us,
+            "how": f"device: {calls} launches replayed from one CUDA graph (L2-resident inputs); "
+                   f"api: {calls} ww.corr_cost_stem3d calls from Python, wall time"}
+
+
+def bench_rows(args, C, ww, cfg, ctx, steps: int) -> dict:
+    """Config 3 split into row bands over the ranks: per step each rank
+    exchanges its one-row halo with its neighbours (NCCL send/recv of
+    [B, C, 1, W] per side, left and right features) and runs the band form of
+    the fused op on its rows.  Value: the whole image's voxels per
+    max-over-ranks step time."""
+    import torch
+    from whirlwind_trt_plugins_b200 import shard
+    x = C.make_inputs_torch(cfg, ctx.dev, seed=3)   # same seed on every rank: one image pair
+    hl = shard.HaloBand(cfg.B, cfg.C, cfg.H, cfg.W, torch.float16, ctx.dev)
+    hr = shard.HaloBand(cfg.B, cfg.C, cfg.H, cfg.W, torch.float16, ctx.dev)
+    hl.own.copy_(x["left"][:, :, hl.r0:hl.r1])
+    hr.own.copy_(x["right"][:, :, hr.r0:hr.r1])
+    w, b = x["w"], x["b"]
+    del x
+    out = torch.empty((cfg.B, cfg.Cout, cfg.D, hl.r1 - hl.r0, cfg.W), dtype=torch.float16, device=ctx.dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        hl.exchange()
+        hr.exchange()
+        ww.corr_cost_stem3d_band(hl.band, hr.band, w, b, cfg.D, cfg.G, cfg.H, hl.i0, hl.r0, hl.r1 - hl.r0,
+                                 act=cfg.act, out=out, stream=stream)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    ms, _ = time_steps(ctx, step, steps, 0.3, False)
+    return {"config": config_dict(cfg, ctx.world, "rows"), "value": cfg.voxels * steps / (ms * 1e-3),
+            "unit": UNIT, "ms_per_step": ms / steps, "scaling": "strong",
+            "gpu_launches": steps, "halo_bytes_per_rank_step": 2 * 2 * cfg.B * cfg.C * cfg.W * 2}
+
+
+def bench_main(args, C, cfg, world, rank, local):
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    ctx = Ctx(world, rank, local)
+    head = bench_config(args, C, ww, cfg, ctx, steps=args.steps, soak_s=1.5, clocks=True,
+                        e2e_steps=max(2, min(args.steps, 5)), cpu_budget_s=10.0)
+    if args.profile:
+        ctx.close()
+        if rank == 0:
+            print(head["profile"], flush=True)
+        return
+    secondary = []
+    if not args.no_secondary:
+        if world == 1:
+            for cid in (2, 3, 5):
+                if cid == cfg_id_of(C, cfg):
+                    continue
+                c2 = C.CONFIGS[cid]
+                r = bench_config(args, C, ww, c2, ctx, steps=max(args.steps, 100), soak_s=0.3, clocks=False,
+                                 e2e_steps=20, cpu_budget_s=6.0)
+                r = {"config": config_dict(c2, world), "unit": UNIT, **r}
+                if cid == 5:
+                    r.update(us_per_call(ww, C, c2, ctx))
+                secondary.append(r)
+        else:
+            secondary.append(bench_rows(args, C, ww, C.CONFIGS[3], ctx, steps=max(args.steps, 50)))
+    ctx.close()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded normal/uniform features, N(0,0.05) weights)",
+        "config": config_dict(cfg, world), "roofline": head["roofline"], "cpu_baseline": head["cpu_baseline"],
+        "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+        "secondary": secondary,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cfg_id_of(C, cfg) -> int:
+    for k, v in C.CONFIGS.items():
+        if v.name == cfg.name:
+            return k
+    return -1
+
+
+# --------------------------------------------------------------- other ops
 
 # Nv12Decode workload: a batch of 720p NV12 camera frames decoded and
 # resized to the plugin's default 224 x 288 output, fp16.
@@ -211,7 +597,6 @@ def bench_nv12(args):
     """One step = ww_nv12_decode over NV12_B frames (one GPU).  value: output
     pixels/s; roofline against HBM with bytes = the whole NV12 input + the
     fp16 output (the downscale reads fewer input bytes than that)."""
-    import numpy as np
     import torch
     import whirlwind_trt_plugins_b200 as ww
     torch.cuda.set_device(0)
@@ -431,191 +816,83 @@ def bench_disparity(args):
     print(json.dumps(line), flush=True)
 
 
-def main():
-    args = parse()
-    if args.op == "nv12_decode":
-        if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            bench_nv12(args)
-        return
-    if args.op == "disparity_regression":
-        if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            bench_disparity(args)
-        return
-    from whirlwind_trt_plugins_b200.configs import CONFIGS
-    cfg = CONFIGS[args.config]
-    if cfg.Cout == 0:
-        raise SystemExit("bench.py measures the fused front end; config %d has no stem" % args.config)
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.impl == "reference":
-        run_reference(args, cfg, rank)
-        return
-
+def bench_stem3_native(args):
+    """The reference's 3-stage CostStem3D at its native shape [1, 1, 48, 32,
+    40] (1 -> 4 -> 4 -> 1, ReLU6), alone (ww_cost_stem3d_ref3) and fused with
+    its G = 1 correlation from C = 64 features (ww_corr_cost_stem3d_ref3):
+    device time per call from a CUDA graph of K launches each."""
     import torch
     import whirlwind_trt_plugins_b200 as ww
-    from whirlwind_trt_plugins_b200.configs import make_inputs_torch
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    # ---- resident inputs: enough rotating sets to exceed L2 ----
-    per_set = cfg.algorithmic_bytes()
-    n_sets = max(2, -(-400 * 2**20 // per_set))  # >= 400 MB in flight
-    n_sets = 1 if args.profile else min(n_sets, 8)
-    sets = []
-    for s in range(n_sets):
-        x = make_inputs_torch(cfg, dev, seed=1000 * rank + 10 * s)
-        out = torch.empty((cfg.B, cfg.Cout, cfg.D, cfg.H, cfg.W), dtype=torch.float16, device=dev)
-        sets.append((x["left"], x["right"], x["w"], x["b"], out))
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    ws = [(torch.randn((n,), generator=g, device="cuda") * s).half()
+          for n, s in ((108, 0.2), (4, 0.1), (432, 0.2), (4, 0.1), (108, 0.2), (1, 0.1))]
+    vol = torch.randn((1, 1, 48, 32, 40), generator=g, device="cuda").half()
+    L = torch.randn((1, 64, 32, 40), generator=g, device="cuda").half()
+    R = torch.randn((1, 64, 32, 40), generator=g, device="cuda").half()
+    out = torch.empty_like(vol)
+    calls = {"stem": lambda s: ww.cost_stem3d_ref3(vol, *ws, out=out, stream=s),
+             "corr_stem": lambda s: ww.corr_cost_stem3d_ref3(L, R, *ws, max_disp=48, out=out, stream=s)}
     stream = torch.cuda.current_stream()
-
-    def step(i):
-        L, R, w, b, out = sets[i % n_sets]
-        ww.corr_cost_stem3d(L, R, w, b, cfg.D, cfg.G, act=cfg.act, out=out, stream=stream)
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
     if args.profile:
-        for i in range(args.steps):
-            step(i)
+        for name in ("stem", "corr_stem"):
+            for _ in range(max(3, args.warmup) + args.steps):
+                calls[name](stream)
         torch.cuda.synchronize()
-        print(f"profile run: {cfg.name}, {args.warmup} + {args.steps} launches of the fused kernel", flush=True)
+        print(f"profile run: stem3_native, {max(3, args.warmup)} + {args.steps} launches of each kernel", flush=True)
         return
-
-    # ---- device-timed value ----
-    with ClockSampler(local) as clk:
-        t_end = time.time() + 1.5          # soak so the sampler sees the clocks under this load
-        i = 0
-        while time.time() < t_end:
-            step(i)
-            i += 1
-            if i % 64 == 0:
-                torch.cuda.synchronize()
+    res = {}
+    for name, fn in calls.items():
+        for _ in range(3):
+            fn(stream)
         torch.cuda.synchronize()
-        barrier()
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.graph(graph, stream=cap):
+            for _ in range(args.steps):
+                fn(torch.cuda.current_stream())
+        stream.wait_stream(cap)
+        graph.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(args.steps):
-            step(i)
+        graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        barrier()
-    clocks = clk.summary()
-    ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_per_step = ms / args.steps
-    vox_step = cfg.voxels * world
-    value = vox_step * args.steps / (ms * 1e-3)
-    if ww.device_error() != 0:
-        raise SystemExit("device error word set during the benchmark")
-
-    # ---- e2e through the public API from host buffers ----
-    # Steps rotate over N_E2E_STREAMS streams, each with its own device and
-    # pinned host buffers, so one step's output copy (device->host) overlaps
-    # the next step's input copy and kernel, as a serving loop would run it.
-    e2e = None
-    if not args.no_e2e:
-        L, R, w, b, out = sets[0]
-        lanes = []
-        for _ in range(N_E2E_STREAMS):
-            hL = torch.empty(L.shape, dtype=L.dtype, pin_memory=True)
-            hR = torch.empty(R.shape, dtype=R.dtype, pin_memory=True)
-            hL.copy_(L)
-            hR.copy_(R)
-            lanes.append({"s": torch.cuda.Stream(dev), "hL": hL, "hR": hR,
-                          "hout": torch.empty(out.shape, dtype=out.dtype, pin_memory=True),
-                          "dL": torch.empty_like(L), "dR": torch.empty_like(R), "dout": torch.empty_like(out)})
-        e2e_steps = max(3, min(args.steps, 60))
-
-        def e2e_step(i):
-            ln = lanes[i % N_E2E_STREAMS]
-            with torch.cuda.stream(ln["s"]):
-                ln["dL"].copy_(ln["hL"], non_blocking=True)
-                ln["dR"].copy_(ln["hR"], non_blocking=True)
-                ww.corr_cost_stem3d(ln["dL"], ln["dR"], w, b, cfg.D, cfg.G, act=cfg.act, out=ln["dout"],
-                                    stream=ln["s"])
-                ln["hout"].copy_(ln["dout"], non_blocking=True)
-
-        for i in range(2 * N_E2E_STREAMS):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        barrier()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for ln in lanes:                      # every lane starts after f0
-            ln["s"].wait_stream(stream)
-        for i in range(e2e_steps):
-            e2e_step(i)
-        for ln in lanes:                      # f1 waits for every lane
-            stream.wait_stream(ln["s"])
-        f1.record(stream)
-        torch.cuda.synchronize()
-        ems = f0.elapsed_time(f1)
-        if dist is not None:
-            t = torch.tensor([ems], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        e2e = {"value": vox_step * e2e_steps / (ems * 1e-3), "unit": UNIT,
-               "h2d_bytes_per_step": (L.numel() + R.numel()) * L.element_size(),
-               "d2h_bytes_per_step": out.numel() * out.element_size(), "steps": e2e_steps,
-               "streams": N_E2E_STREAMS}
-
-    # ---- roofline of the fused kernel (the only kernel in a step) ----
-    peaks = load_peaks()
-    t_launch = ms_per_step * 1e-3
-    tflops = cfg.stem_flops() / t_launch / 1e12
-    gbs = cfg.algorithmic_bytes() / t_launch / 1e9
-    traffic = NCU_TRAFFIC_BYTES.get(cfg.name)
-    f_tc, f_hbm = tflops / peaks["tflops"], gbs / peaks["hbm_gbs"]
-    if f_tc >= f_hbm:
-        roof = {"bound": "tensor", "achieved": tflops, "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": f_tc}
-    else:
-        roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": f_hbm}
-    roof.update({"traffic": traffic, "peak_source": peaks["src"],
-                 "other": {"hbm_gbs": gbs, "hbm_frac": f_hbm, "tensor_tflops": tflops, "tensor_frac": f_tc}})
-
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-
-    cpu = None
-    if not args.no_cpu_baseline and world == 1:
-        try:
-            cpu = cpu_baseline(cfg)
-        except Exception as e:  # the baseline never blocks the measurement
-            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {e}"}
-
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded normal/uniform features, N(0,0.05) weights)",
-        "config": {"workload": f"{cfg.name}: B={cfg.B} C={cfg.C} G={cfg.G} H={cfg.H} W={cfg.W} D={cfg.D} "
-                               f"Cout={cfg.Cout} fp16", "global_batch": cfg.B * world,
-                   "parallelism": f"batch-sharded replicas x{world} (no collective in the op)",
-                   "l2": f"{n_sets} rotating input/output sets, {n_sets * per_set / 2**20:.0f} MB > 126 MB L2"},
-        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-        "clocks": clocks,
-    }
+        res[name] = e0.elapsed_time(e1) * 1e3 / args.steps
+        del graph
+    vox = 48 * 32 * 40
+    line = {"metric": "cost voxels/s, reference 3-stage CostStem3D at its native shape", "unit": UNIT,
+            "value": vox / (res["stem"] * 1e-6), "us_per_call": res["stem"],
+            "corr_stem_us_per_call": res["corr_stem"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "CostStem3D [1,1,48,32,40] (and CorrVolume G=1 from C=64 fused with it)",
+                       "timing": "K launches replayed from one CUDA graph, L2-resident"},
+            "gpu_launches": args.steps}
     print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.op != "corr_cost_stem3d":
+        if rank == 0 and args.impl == "ours":
+            {"nv12_decode": bench_nv12, "disparity_regression": bench_disparity,
+             "stem3_native": bench_stem3_native}[args.op](args)
+        return
+    C = load_configs()
+    cfg = C.CONFIGS[args.config]
+    if cfg.Cout == 0:
+        raise SystemExit("bench.py measures the fused front end; config %d has no stem" % args.config)
+    if args.batch:
+        cfg = cfg.scaled(B=args.batch)
+    if args.impl == "reference":
+        run_reference(args, C, cfg, rank, world)
+        return
+    bench_main(args, C, cfg, world, rank, local)
 
 
 if __name__ == "__main__":

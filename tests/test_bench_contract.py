@@ -35,3 +35,27 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_reference_arm_loads_nothing_from_the_package():
+    """The reference arm must not import the product package or map its CUDA
+    library, and prints the same config dict as the GPU arm (config_dict)."""
+    code = (
+        "import json, runpy, sys, io, contextlib\n"
+        f"sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '1']\n"
+        "buf = io.StringIO()\n"
+        "with contextlib.redirect_stdout(buf):\n"
+        f"    runpy.run_path({os.path.join(ROOT, 'bench.py')!r}, run_name='__main__')\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "assert 'libww_trt_plugins' not in maps, 'library mapped'\n"
+        "assert 'whirlwind_trt_plugins_b200' not in sys.modules, 'package imported'\n"
+        "line = json.loads(buf.getvalue().strip().splitlines()[-1])\n"
+        f"sys.path.insert(0, {ROOT!r})\n"
+        "import bench\n"
+        "C = bench.load_configs()\n"
+        "assert line['config'] == bench.config_dict(C.CONFIGS[bench.DEFAULT_CONFIG], 1), line['config']\n"
+        "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=dict(os.environ, RANK="0", WORLD_SIZE="1"),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip().endswith("ok")

@@ -167,15 +167,48 @@ def test_fused_shapes_match_oracle(ww, torch, orc, shape):
     assert ww.device_error() == 0
 
 
-@pytest.mark.parametrize("cfg_id", [2, 5])
-def test_fused_full_size_matches_oracle(ww, torch, orc, cfg_id):
+@pytest.mark.parametrize("cfg_id,B", [(2, 1), (3, 4), (4, 1), (4, 2), (5, 2)])
+def test_fused_full_size_matches_oracle(ww, torch, orc, cfg_id, B):
+    """The benchmark configurations at their full H x W x D (and full batch,
+    except config 4, whose 64 items are checked as B = 1 and B = 2 with the
+    5 % zeroed-pixel mask): every output within the fp16 tolerance of the
+    oracle (fp32 sequential accumulation), and the fused volume within one
+    fp16 ulp of the unfused CorrVolume -> stem composition."""
     from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
-    cfg = CONFIGS[cfg_id]
+    cfg = CONFIGS[cfg_id].scaled(B=B)
     x = make_inputs(cfg)
-    out = _fused(ww, torch, x, cfg).cpu().numpy().astype(np.float32)
-    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=orc.ACC_F32_SEQ)
-    err = np.abs(out - ref.astype(np.float32)).max()
-    assert err <= ATOL_F16, f"max abs err {err}"
+    t = {k: _t(torch, x[k]) for k in ("left", "right", "w", "b")}
+    fused = ww.corr_cost_stem3d(t["left"], t["right"], t["w"], t["b"], cfg.D, cfg.G, act=cfg.act)
+    out = fused.cpu().numpy().astype(np.float32)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, act=cfg.act,
+                        acc_mode=orc.ACC_F32_SEQ).astype(np.float32)
+    err = np.abs(out - ref)
+    assert float(err.max()) <= ATOL_F16, f"max abs err {err.max()} at {np.unravel_index(err.argmax(), err.shape)}"
+    assert np.all(np.isfinite(out))
+    vol = ww.corr_volume(t["left"], t["right"], cfg.D, cfg.G)
+    unfused = ww.cost_stem3d(vol, t["w"], t["b"], act=cfg.act)
+    diff = (fused.float() - unfused.float()).abs()
+    assert float(diff.max()) <= ATOL_F16
+    assert float((diff == 0).float().mean()) >= 0.99
+    assert ww.device_error() == 0
+
+
+def test_fused_band_stitches_full_width(ww, torch):
+    """Row bands of a full-width config-3 image (W = 320, D = 64): four bands
+    of uneven height, each from its rows plus the one-row halo, stitch to the
+    unsharded output bit for bit."""
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[3].scaled(B=1)
+    x = make_inputs(cfg)
+    tl, tr, tw, tb = (_t(torch, x[k]) for k in ("left", "right", "w", "b"))
+    full = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+    parts = []
+    for (r0, r1) in ((0, 45), (45, 46), (46, 113), (113, 180)):
+        i0, i1 = max(0, r0 - 1), min(cfg.H, r1 + 1)
+        parts.append(ww.corr_cost_stem3d_band(tl[:, :, i0:i1].contiguous(), tr[:, :, i0:i1].contiguous(), tw, tb,
+                                              cfg.D, cfg.G, cfg.H, i0, r0, r1 - r0))
+    stitched = torch.cat(parts, dim=3)
+    assert torch.equal(stitched.view(torch.int16), full.view(torch.int16))
 
 
 def test_fused_band_stitches_to_full(ww, torch):

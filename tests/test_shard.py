@@ -184,3 +184,37 @@ def _bad_shape_worker(rank, world, port, outdir):
             f.write(res)
     finally:
         dist.destroy_process_group()
+
+
+def _haloband_worker(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch
+    from whirlwind_trt_plugins_b200 import shard
+    dist = _init(rank, world, port)
+    try:
+        s = SHAPE
+        L, _, _, _ = _inputs()
+        hb = shard.HaloBand(s["B"], s["C"], s["H"], s["W"], torch.float16, "cpu")
+        hb.own.copy_(torch.from_numpy(np.ascontiguousarray(L[:, :, hb.r0:hb.r1])))
+        for _ in range(2):  # repeated exchanges reuse the same buffers
+            hb.exchange()
+        np.save(os.path.join(outdir, f"hb{rank}.npy"), hb.band.numpy())
+        with open(os.path.join(outdir, f"hb{rank}.txt"), "w") as f:
+            f.write(f"{hb.i0} {hb.i1}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_haloband_holds_rows_and_halo(tmp_path, world):
+    codes = _run(world, _haloband_worker, (str(tmp_path),))
+    assert codes == [0] * world, codes
+    L, _, _, _ = _inputs()
+    from whirlwind_trt_plugins_b200.shard import split_even, halo_rows
+    for r in range(world):
+        i0, i1 = (int(v) for v in (tmp_path / f"hb{r}.txt").read_text().split())
+        r0, r1 = split_even(SHAPE["H"], world, r)
+        assert (i0, i1) == halo_rows(SHAPE["H"], r0, r1)
+        band = np.load(tmp_path / f"hb{r}.npy")
+        assert np.array_equal(band.view(np.uint16), L[:, :, i0:i1].view(np.uint16))

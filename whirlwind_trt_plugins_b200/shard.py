@@ -23,7 +23,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-__all__ = ["split_even", "halo_rows", "exchange_halo", "corr_cost_stem3d_rows",
+__all__ = ["split_even", "halo_rows", "exchange_halo", "HaloBand", "corr_cost_stem3d_rows",
            "corr_cost_stem3d_batch", "gather_rows"]
 
 
@@ -86,6 +86,53 @@ def exchange_halo(x_local: torch.Tensor, H: int, group=None) -> tuple[torch.Tens
     if bot is not None:
         band[:, :, -1:].copy_(bot)
     return band, i0
+
+
+class HaloBand:
+    """A rank's persistent row band of one feature map, for repeated
+    row-sharded calls: ``band`` [B, C, i1 - i0, W] holds image rows
+    [i0, i1) = ``halo_rows(H, r0, r1)``; the caller (e.g. the feature network)
+    writes its own rows [r0, r1) into ``own`` once per frame, and
+    ``exchange()`` fetches only the two halo rows from the neighbours (one
+    contiguous [B, C, 1, W] message per side and direction) and writes them
+    into the band's edge rows.  Nothing is allocated per call."""
+
+    def __init__(self, B: int, C: int, H: int, W: int, dtype, device, group=None):
+        world, rank = _world(group)
+        if H < world:
+            raise ValueError("row sharding needs at least one image row per rank")
+        self.group, self.world, self.rank, self.H = group, world, rank, H
+        self.r0, self.r1 = split_even(H, world, rank)
+        self.i0, self.i1 = halo_rows(H, self.r0, self.r1)
+        self.band = torch.zeros((B, C, self.i1 - self.i0, W), dtype=dtype, device=device)
+        self.own = self.band[:, :, self.r0 - self.i0:self.r1 - self.i0]
+        row = (B, C, 1, W)
+        self._send_top = torch.empty(row, dtype=dtype, device=device) if rank > 0 else None
+        self._recv_top = torch.empty(row, dtype=dtype, device=device) if rank > 0 else None
+        self._send_bot = torch.empty(row, dtype=dtype, device=device) if rank < world - 1 else None
+        self._recv_bot = torch.empty(row, dtype=dtype, device=device) if rank < world - 1 else None
+
+    def exchange(self) -> None:
+        ops = []
+        k0 = self.r0 - self.i0  # band index of the first own row
+        k1 = self.r1 - self.i0  # one past the last own row
+        if self._send_top is not None:
+            self._send_top.copy_(self.band[:, :, k0:k0 + 1])
+            peer = _peer(self.group, self.rank - 1)
+            ops.append(dist.P2POp(dist.isend, self._send_top, peer, self.group))
+            ops.append(dist.P2POp(dist.irecv, self._recv_top, peer, self.group))
+        if self._send_bot is not None:
+            self._send_bot.copy_(self.band[:, :, k1 - 1:k1])
+            peer = _peer(self.group, self.rank + 1)
+            ops.append(dist.P2POp(dist.isend, self._send_bot, peer, self.group))
+            ops.append(dist.P2POp(dist.irecv, self._recv_bot, peer, self.group))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        if self._recv_top is not None:
+            self.band[:, :, :1].copy_(self._recv_top)
+        if self._recv_bot is not None:
+            self.band[:, :, -1:].copy_(self._recv_bot)
 
 
 def _default_band_fn():

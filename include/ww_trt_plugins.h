@@ -139,6 +139,49 @@ int ww_corr_cost_stem3d_band(const void* left, const void* right, const void* w,
                              void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Multi-device driver of ww_corr_cost_stem3d (extension; the reference has no
+ * multi-GPU code).  One host thread, n parts,
+ * part k on device devices[k] with stream streams[k] (streams NULL: the
+ * legacy default stream of each device).  Several parts may use the same
+ * device.  Asynchronous: returns once everything is enqueued.
+ *   WW_MULTI_BATCH  part k holds batch items [b0, b1) = split_even(B, n, k)
+ *                   (the first B % n parts get one more): left[k], right[k]
+ *                   [b1 - b0, C, H, W] -> out[k] [b1 - b0, Cout, D, H, W];
+ *                   nothing moves between devices.
+ *   WW_MULTI_ROWS   one image split by rows: part k owns rows [r0, r1) and
+ *                   holds them in a band buffer left[k], right[k]
+ *                   [B, C, i1 - i0, W] of rows [i0, i1) (ww_multi_split: one
+ *                   halo row each side, clipped).  The caller fills the own
+ *                   rows; the driver copies each halo row from the
+ *                   neighbour's band (one strided cudaMemcpy3DPeerAsync per
+ *                   row and tensor, on streams[k], after everything already
+ *                   enqueued on the neighbour's stream), then runs the band
+ *                   form: out[k] [B, Cout, D, r1 - r0, W].  Work enqueued
+ *                   afterwards on a part's stream waits for the neighbours'
+ *                   copies out of its rows.  The stitched rows equal
+ *                   ww_corr_cost_stem3d on the whole image bit for bit.
+ * w[k] [Cout, G, 3, 3, 3] and b[k] [Cout]: the weights, on device k.
+ * Returns 0 or the first failing status (a failed copy: WW_ERR_LAUNCH with
+ * the CUDA message on stderr); work enqueued before a failure stays enqueued.
+ * ------------------------------------------------------------------------- */
+#define WW_MULTI_BATCH 0
+#define WW_MULTI_ROWS 1
+int ww_corr_cost_stem3d_multi(int n, const int* devices, int mode, void* const* left, void* const* right,
+                              const void* const* w, const void* const* b, void* const* out, int B, int C, int G,
+                              int H, int W, int D, int Cout, int act, void* const* streams);
+
+/* Row partition of the multi-device driver (host only): part k of n owns
+ * image rows [r0, r1) of H (the first H % n parts get one more) and needs
+ * the band [i0, i1) = [max(r0 - 1, 0), min(r1 + 1, H)).  Needs H >= n. */
+int ww_multi_split(int n, int H, int k, int* r0, int* r1, int* i0, int* i1);
+
+/* Fault injection for tests (host side): after `after_n_copies` more halo
+ * copies, the next one the driver would issue fails with
+ * cudaErrorInvalidValue instead of being enqueued (once); negative
+ * disables.  The process-wide setting also affects concurrent callers. */
+int ww_multi_inject_copy_failure(int after_n_copies);
+
+/* ---------------------------------------------------------------------------
  * CorrVolume (G = 1) fused with the reference's 3-stage CostStem3D, the pair
  * the reference runs at its native shape ([1, 1, 48, 32, 40]):
  *   out = ww_cost_stem3d_ref3(ww_corr_volume(left, right, D), w0 .. b2)

@@ -18,6 +18,8 @@ reference project):
 * ``cost_stem3d(vol, w, b, act)``                      -- generalised 3-input stem
 * ``corr_cost_stem3d(left, right, w, b, max_disp, num_groups, act)`` -- fused op
 * ``corr_cost_stem3d_band(...)``                       -- row-band form for sharding
+* ``corr_cost_stem3d_multi(...)``                      -- several devices from one thread
+  (batch split, or row bands with the halo rows copied between devices)
 * ``nv12_decode(nv12, out_h, out_w, dtype)``           -- Nv12Decode
   (``src/plugins/nv12_decode/nv12_decode_kernel.hpp:20-28``)
 * ``disparity_regression(cost, mode, dtype)``          -- soft-argmax / soft-argmin
@@ -36,6 +38,7 @@ __all__ = [
     "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "corr_cost_stem3d_ref3", "cost_stem3d",
     "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "disparity_regression", "fold_bn", "device_error",
     "clear_device_error", "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF", "DISP_SOFTARGMAX", "DISP_SOFTARGMIN",
+    "MULTI_BATCH", "MULTI_ROWS", "multi_split", "corr_cost_stem3d_multi",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libww_trt_plugins.so")
@@ -46,6 +49,8 @@ ACT_RELU = 0
 ACT_RELU6 = 1
 DISP_SOFTARGMAX = 0
 DISP_SOFTARGMIN = 1
+MULTI_BATCH = 0
+MULTI_ROWS = 1
 
 STATUS = {
     0: "success", 1: "CUDA launch or runtime call failed", 2: "invalid tensor shape",
@@ -79,6 +84,9 @@ def _load() -> ctypes.CDLL:
     L.ww_nv12_decode.argtypes = [p, p] + [i] * 6 + [p]
     L.ww_disparity_regression.argtypes = [p, p] + [i] * 7 + [p]
     L.ww_fold_bn_f16.argtypes = [p, p, p, i, i, p, p]
+    L.ww_corr_cost_stem3d_multi.argtypes = [i, p, i, p, p, p, p, p] + [i] * 8 + [p]
+    L.ww_multi_split.argtypes = [i, i, i] + [ctypes.POINTER(ctypes.c_int)] * 4
+    L.ww_multi_inject_copy_failure.argtypes = [i]
     L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.ww_clear_device_error.argtypes = []
     del f
@@ -255,6 +263,77 @@ def corr_cost_stem3d_band(left_band, right_band, w, b, max_disp: int, num_groups
         B, C, num_groups, H, W, max_disp, Cout, act, in_row0, in_rows, out_row0, out_rows,
         _stream_ptr(stream)))
     return out
+
+
+def multi_split(n: int, H: int, k: int) -> tuple[int, int, int, int]:
+    """Rows (r0, r1) of part k of n in an H-row image and the band (i0, i1)
+    it holds (one halo row each side, clipped): ww_multi_split."""
+    v = [ctypes.c_int(0) for _ in range(4)]
+    _check("ww_multi_split", _lib.ww_multi_split(n, H, k, *[ctypes.byref(x) for x in v]))
+    return tuple(x.value for x in v)
+
+
+def corr_cost_stem3d_multi(lefts, rights, ws, bs, max_disp: int, num_groups: int, mode: int = MULTI_BATCH,
+                           act: int = ACT_RELU, H: int | None = None, outs=None, streams=None):
+    """The fused op over several parts (each a CUDA tensor set on its own
+    device; parts may share a device) through ww_corr_cost_stem3d_multi.
+
+    MULTI_BATCH: lefts[k]/rights[k] [b_k, C, H, W] hold batch items
+    split_even(B, n, k); returns outs[k] [b_k, Cout, D, H, W].
+    MULTI_ROWS: lefts[k]/rights[k] [B, C, i1 - i0, W] are band buffers of an
+    H-row image (multi_split) with the own rows filled; the halo rows are
+    copied from the neighbours by the library; returns outs[k]
+    [B, Cout, D, r1 - r0, W].  streams[k]: a torch stream of part k's device
+    (default: its current stream)."""
+    torch = _torch()
+    n = len(lefts)
+    if not (len(rights) == len(ws) == len(bs) == n) or n == 0:
+        raise ValueError("one left, right, w and b per part")
+    if mode not in (MULTI_BATCH, MULTI_ROWS):
+        raise ValueError("mode must be MULTI_BATCH or MULTI_ROWS")
+    for k in range(n):
+        for t, nm in ((lefts[k], "left"), (rights[k], "right"), (ws[k], "w"), (bs[k], "b")):
+            _dev(t, f"{nm}[{k}]", torch.float16)
+        if lefts[k].dim() != 4 or lefts[k].shape != rights[k].shape:
+            raise ValueError(f"left[{k}] and right[{k}] must both be [B, C, rows, W]")
+        if not (lefts[k].device == rights[k].device == ws[k].device == bs[k].device):
+            raise ValueError(f"part {k}: left, right, w and b must be on one device")
+    C, W = lefts[0].shape[1], lefts[0].shape[3]
+    Cout = bs[0].numel()
+    if any(t.numel() != Cout * num_groups * 27 for t in ws):
+        raise ValueError("w must be [Cout, num_groups, 3, 3, 3]")
+    shapes = []
+    if mode == MULTI_BATCH:
+        H = lefts[0].shape[2]
+        B = sum(t.shape[0] for t in lefts)
+        for k in range(n):
+            base, extra = divmod(B, n)
+            bk = base + (1 if k < extra else 0)
+            if lefts[k].shape != (bk, C, H, W):
+                raise ValueError(f"part {k} must hold {bk} of the {B} pairs: [{bk}, {C}, {H}, {W}]")
+            shapes.append((bk, Cout, max_disp, H, W))
+    else:
+        if H is None:
+            raise ValueError("MULTI_ROWS needs the image height H")
+        B = lefts[0].shape[0]
+        for k in range(n):
+            r0, r1, i0, i1 = multi_split(n, H, k)
+            if lefts[k].shape != (B, C, i1 - i0, W):
+                raise ValueError(f"part {k} must hold rows [{i0}, {i1}): [{B}, {C}, {i1 - i0}, {W}]")
+            shapes.append((B, Cout, max_disp, r1 - r0, W))
+    if outs is None:
+        outs = [None] * n
+    outs = [_out(outs[k], shapes[k], torch.float16, lefts[k].device, f"out[{k}]") for k in range(n)]
+    if streams is None:
+        streams = [torch.cuda.current_stream(t.device) for t in lefts]
+    P = ctypes.c_void_p * n
+    devs = (ctypes.c_int * n)(*[t.device.index for t in lefts])
+    sp = P(*[s.cuda_stream if hasattr(s, "cuda_stream") else int(s) for s in streams])
+    _check("ww_corr_cost_stem3d_multi", _lib.ww_corr_cost_stem3d_multi(
+        n, devs, mode, P(*[t.data_ptr() for t in lefts]), P(*[t.data_ptr() for t in rights]),
+        P(*[t.data_ptr() for t in ws]), P(*[t.data_ptr() for t in bs]), P(*[t.data_ptr() for t in outs]),
+        B, C, num_groups, H, W, max_disp, Cout, act, sp))
+    return outs
 
 
 def nv12_decode(nv12, out_h: int = 224, out_w: int = 288, dtype=None, out=None, stream=None):

@@ -37,6 +37,7 @@ SOURCES = [
     "tensor_map.cu",
     "nv12_decode.cu",
     "disparity_regression.cu",
+    "multi.cu",
     "plugin_core.cpp",
 ]
 TRT_SOURCES = ["trt/ww_trt_plugins.cpp"]

@@ -553,11 +553,15 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     const int lane = threadIdx.x & 31;
 
     // ---- tile coordinates ----
+    // Adjacent column tiles of one strip are consecutive CTAs, so they run
+    // at the same time: the halves of each 32-byte output sector that two
+    // neighbouring tiles write meet in L2, and so do their overlapping
+    // right-feature windows.
     int t = blockIdx.x;
-    const int strip = t % p.n_strips;
-    t /= p.n_strips;
     const int wt = t % p.n_wtiles;
-    const int b = t / p.n_wtiles;
+    t /= p.n_wtiles;
+    const int strip = t % p.n_strips;
+    const int b = t / p.n_strips;
     const int w0 = wt * kWt;
     const int r0 = p.out_row0 + strip * p.strip;                    // first output row
     const int r1 = min(r0 + p.strip, p.out_row0 + p.out_rows);     // one past last

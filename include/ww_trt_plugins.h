@@ -126,6 +126,21 @@ int ww_corr_cost_stem3d(const void* left, const void* right, const void* w, cons
                         void* out, int B, int C, int G, int H, int W, int D, int Cout,
                         int act, void* stream);
 
+/* Limits of ww_corr_cost_stem3d / _band / _multi and of ww_cost_stem3d
+ * (this build): Cout <= 32; D <= 80 when Cout > 16 and D <= 160 when
+ * Cout <= 16 (three Cout-column tensor-memory accumulators per 16
+ * disparities within 512 columns); G (or Cin) <= 56 (at most 32 K-steps of
+ * two 8-group chunks); and the weights, two volume rows and two staging
+ * slots within the device's shared memory, which bounds G further: on a
+ * B200 with C / G = 8 the largest G is 48, 40, 32, 24 for Cout 17..32 and
+ * D = 32, 48, 64, 80, and 56, 56, 40, 40, 32, 24, 16 for Cout <= 16 and
+ * D = 32, 48, 64, 80, 96, 128, 160.  Shapes outside them return
+ * WW_ERR_UNSUPPORTED.  These two functions answer without launching
+ * anything (0, WW_ERR_INVALID_SHAPE or WW_ERR_UNSUPPORTED), using the current
+ * device's shared memory, or a B200's when no usable device is current. */
+int ww_corr_cost_stem3d_supported(int C, int G, int D, int Cout);
+int ww_cost_stem3d_supported(int Cin, int D, int Cout);
+
 /* Row-band form of ww_corr_cost_stem3d for sharding one image pair across
  * devices.  `left`/`right` hold image rows [in_row0, in_row0 + in_rows) of an
  * H-row image ([B, C, in_rows, W]); `out` receives rows
@@ -271,7 +286,9 @@ int ww_plugin_cost_stem3d_enqueue(int nb_inputs, int act, const ww_tensor_desc_t
 
 /* "CorrCostStem3D" v"1" (extension): fields max_disp (48), num_groups (1),
  * act (0 ReLU, 1 ReLU6); inputs left, right [B,C,H,W], w [Cout,G,3,3,3], b [Cout];
- * output [B, Cout, max_disp, H, W]; fp16 only.  With 8 inputs (left, right,
+ * output [B, Cout, max_disp, H, W]; fp16 only.  output_dims returns 1 for a
+ * shape outside ww_corr_cost_stem3d_supported (so an engine build fails,
+ * not the enqueue) and when the weights' group count is not num_groups.  With 8 inputs (left, right,
  * w0, b0, w1, b1, w2, b2; num_groups 1) it is ww_corr_cost_stem3d_ref3 and
  * the output is [B, 1, max_disp, H, W]. */
 int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_inputs,

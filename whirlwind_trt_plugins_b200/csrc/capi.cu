@@ -18,6 +18,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                    const void* b, void* out, int B, int C, int G, int H, int W, int D, int Cout,
                    int act, int in_row0, int in_rows, int out_row0, int out_rows,
                    cudaStream_t stream) noexcept;
+int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept;
 int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT,
                        int W_OUT, cudaStream_t stream) noexcept;
 int disparity_regression_launch(const void* cost, void* out, int in_dtype, int out_dtype, int B, int D, int H,
@@ -102,6 +103,26 @@ int ww_corr_volume(const void* left, const void* right, void* out, int dtype, in
 {
     return ww::corr_volume_launch(left, right, out, dtype, B, C, H, W, D, G,
                                   static_cast<cudaStream_t>(stream));
+}
+
+// Opt-in shared memory per block of the current device, or of a B200 when
+// no usable device is current (a host checking shapes without a GPU).
+static int smem_optin_or_b200() noexcept
+{
+    ww::DeviceInfo d;
+    if (ww::current_device_info(&d) == WW_SUCCESS) return d.smem_optin;
+    cudaGetLastError();
+    return 232448;
+}
+
+int ww_corr_cost_stem3d_supported(int C, int G, int D, int Cout)
+{
+    return ww::stem_limits(true, C, G, D, Cout, smem_optin_or_b200());
+}
+
+int ww_cost_stem3d_supported(int Cin, int D, int Cout)
+{
+    return ww::stem_limits(false, Cin, Cin, D, Cout, smem_optin_or_b200());
 }
 
 int ww_cost_stem3d_ref3(const void* in, void* out, const void* w0, const void* b0, const void* w1,

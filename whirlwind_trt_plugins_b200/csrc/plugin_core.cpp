@@ -133,6 +133,11 @@ int ww_plugin_cost_stem3d_output_dims(int nb_inputs, const ww_tensor_desc_t* inp
     }
     if (nb_inputs == 3) {
         if (inputs[0].nb_dims != 5 || inputs[1].nb_dims != 5) return 1;
+        // the generalised stem's limits (ww_cost_stem3d_supported), where known
+        const int64_t Cin = inputs[0].dims[1], D = inputs[0].dims[2], Cout = inputs[1].dims[0];
+        if (Cin > 0 && D > 0 && Cout > 0 && fits_int(Cin) && fits_int(D) && fits_int(Cout) &&
+            ww_cost_stem3d_supported(static_cast<int>(Cin), static_cast<int>(D), static_cast<int>(Cout)) != WW_SUCCESS)
+            return 1;
         *out = inputs[0];
         out->dims[1] = inputs[1].dims[0];
         return 0;
@@ -183,10 +188,21 @@ int ww_plugin_cost_stem3d_enqueue(int nb_inputs, int act, const ww_tensor_desc_t
 int ww_plugin_corr_cost_stem3d_output_dims(int max_disp, int num_groups, int nb_inputs,
                                            const ww_tensor_desc_t* inputs, ww_tensor_desc_t* out)
 {
-    (void)num_groups;
     if ((nb_inputs != 4 && nb_inputs != 8) || inputs == nullptr || out == nullptr) return 1;
     if (inputs[0].nb_dims != 4) return 1;
-    if (nb_inputs == 4 && inputs[2].nb_dims != 5) return 1;
+    if (nb_inputs == 4) {
+        // The fused kernel's limits, checked here so that an engine build
+        // fails rather than the enqueue (C may be unknown, -1, for a dynamic
+        // shape: then the group-size dependent part is left to the enqueue).
+        if (inputs[2].nb_dims != 5) return 1;
+        const int G = num_groups <= 0 ? 1 : num_groups;
+        if (inputs[2].dims[1] != G || !fits_int(inputs[2].dims[0])) return 1;
+        const int Cout = static_cast<int>(inputs[2].dims[0]);
+        const int64_t C = inputs[0].dims[1];
+        const int lim = C > 0 && fits_int(C) ? ww_corr_cost_stem3d_supported(static_cast<int>(C), G, max_disp, Cout)
+                                             : ww_corr_cost_stem3d_supported(8 * G, G, max_disp, Cout);
+        if (lim != WW_SUCCESS) return 1;
+    }
     *out = inputs[0];
     out->nb_dims = 5;
     out->dims[0] = inputs[0].dims[0];

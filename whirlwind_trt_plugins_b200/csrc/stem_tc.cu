@@ -1066,6 +1066,45 @@ uint32_t pow2_cols(uint32_t c)
 
 }  // namespace
 
+// Whether the stem kernel takes a shape: WW_SUCCESS, WW_ERR_INVALID_SHAPE or
+// WW_ERR_UNSUPPORTED (the limits of this build: Cout <= 32; the stem's
+// accumulators -- three Cout-column slots per 16-disparity M-block -- within
+// the 512 tensor-memory columns, i.e. D <= 80 for Cout 17..32 and D <= 160
+// for Cout <= 16; at most kMaxSteps K-steps, i.e. G <= 56; and the smallest
+// shared-memory layout -- B image, two volume-row buffers, two staging slots
+// -- within smem_optin bytes).  fused: the correlation feeds the stem (C
+// channels in G groups); otherwise a G-channel volume is read.
+int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept
+{
+    if (C <= 0 || G <= 0 || D <= 0 || Cout <= 0) return WW_ERR_INVALID_SHAPE;
+    if (fused && C % G != 0) return WW_ERR_INVALID_SHAPE;
+    if (Cout > 32) return WW_ERR_UNSUPPORTED;
+    const int coutp = Cout <= 16 ? 16 : 32;
+    const int KG = (G + 7) / 8;
+    const int Dp = (D + 15) / 16 * 16;
+    const int n_mb = Dp / 16;
+    if (n_mb * 3 * coutp > 512 || n_mb > kMaxMB) return WW_ERR_UNSUPPORTED;
+    const int nsteps = 9 * (KG / 2) + ((KG & 1) ? 5 : 0);
+    if (nsteps > kMaxSteps) return WW_ERR_UNSUPPORTED;
+    const long long Cg = fused ? C / G : 1;
+    const long long vol_buf = static_cast<long long>(Dp + 2) * kWtp * 16 * KG + 128;
+    long long o = static_cast<long long>(nsteps) * 2 * 5 * coutp * 16;
+    o = (o + 127) & ~127LL;
+    o += 2 * vol_buf;
+    o = (o + 127) & ~127LL;
+    o += 128 + (2 * kMaxVBuf + 1 + 2 * kMaxSlots + 2) * 8 + 16;
+    o = (o + 15) & ~15LL;
+    o += coutp * 4;
+    o = (o + 1023) & ~1023LL;
+    if (fused) {
+        const long long rstage_w = 16 + 8 * ((D + 7) / 8);
+        const long long n_rbox = (rstage_w + 63) / 64;
+        const long long slot = ((n_rbox * 8 * Cg * 128 + 8 * Cg * kLRowBytes + 1023) / 1024) * 1024;
+        o += 2 * slot;
+    }
+    return o <= smem_optin ? WW_SUCCESS : WW_ERR_UNSUPPORTED;
+}
+
 int stem_tc_launch(const void* vol, const void* left, const void* right, const void* w, const void* b,
                    void* out, int B, int C, int G, int H, int W, int D, int Cout, int act, int in_row0,
                    int in_rows, int out_row0, int out_rows, cudaStream_t stream) noexcept
@@ -1088,6 +1127,10 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
 
     DeviceInfo dev;
     if (current_device_info(&dev) != WW_SUCCESS || dev.cc_major < 10) return WW_ERR_DEVICE;
+    {
+        const int lim = stem_limits(fused, C, G, D, Cout, dev.smem_optin);
+        if (lim != WW_SUCCESS) return lim;
+    }
 
     const int coutp = Cout <= 16 ? 16 : 32;
     const int KG = (G + 7) / 8;

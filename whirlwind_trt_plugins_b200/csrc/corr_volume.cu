@@ -137,6 +137,20 @@ __device__ __forceinline__ void stage_rows(T* __restrict__ dst, const T* __restr
     else stage_rows_batched<T, 8>(dst, src_row0, chan_stride, nc, col0, width, W, vec_ok);
 }
 
+__device__ __forceinline__ void unpack_h2(uint32_t x, unsigned short& lo, unsigned short& hi)
+{
+    asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(x));
+}
+
+// fp32 a * b + c of two fp16 operands with one rounding (the product is
+// exact in fp32): the same value as fmaf(float(a), float(b), c).
+__device__ __forceinline__ float fma_h(unsigned short a, unsigned short b, float c)
+{
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+    return d;
+}
+
 template <typename T, int TW, int CC>
 __global__ void __launch_bounds__(256) corr_volume_kernel(
     const T* __restrict__ left, const T* __restrict__ right, T* __restrict__ out,
@@ -212,6 +226,111 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
         if (gx + kVecW <= W && (reinterpret_cast<uintptr_t>(op) % (kVecW * sizeof(T))) == 0) {
             if constexpr (sizeof(T) == 2) *reinterpret_cast<uint2*>(op) = *reinterpret_cast<uint2*>(tmp);
             else *reinterpret_cast<uint4*>(op) = *reinterpret_cast<uint4*>(tmp);
+        } else {
+#pragma unroll
+            for (int v = 0; v < kVecW; ++v)
+                if (gx + v < W) op[v] = tmp[v];
+        }
+    }
+}
+
+// fp16 images wider than 64 columns.  Same register tile (4 columns x 8
+// disparities per thread, fp32 fma chains in channel order from +0) as
+// corr_volume_kernel, with three changes that cut the instructions per fma
+// from about two to about one:
+//   * the column tile is sized to the image (tw = W / ceil(W / 256) rounded
+//     up to 16: one 160-column tile for W = 160, two for W = 312), not fixed
+//     at 128 columns, which left most of a second tile idle;
+//   * per channel the 4 left and 11 right operands come in as one and three
+//     8-byte shared loads (the right ones from the 4-aligned position one
+//     before the first needed);
+//   * the fma takes the fp16 operands directly (fma.rn.f32.f16: the product
+//     of two fp16 values is exact in fp32, so the result is identical to
+//     converting them first), so no conversions are issued.
+// blockDim = (tw / 4, ny), ny * 8 = DT disparities per CTA.
+template <int CC>
+__global__ void __launch_bounds__(512) corr_volume_h_kernel(
+    const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
+    int C, int H, int W, int D, int G, int n_dband, int tw, int scale_div, float inv_cg, int vec_ok)
+{
+    constexpr int ND = kDispPerThread;
+    const int DT = ND * blockDim.y;
+    const int RW = tw + DT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half* Ls = reinterpret_cast<__half*>(smem_raw);
+    __half* Rs = Ls + CC * tw;
+
+    const int w0 = blockIdx.x * tw;
+    const int h = blockIdx.y / n_dband;
+    const int d0 = (blockIdx.y - h * n_dband) * DT;
+    const int b = blockIdx.z / G;
+    const int g = blockIdx.z - b * G;
+    const int Cg = C / G;
+
+    const int64_t plane = i64(H) * W;
+    const __half* lrow = left + (i64(b) * C + i64(g) * Cg) * plane + i64(h) * W;
+    const __half* rrow = right + (i64(b) * C + i64(g) * Cg) * plane + i64(h) * W;
+
+    const int wl = threadIdx.x * kVecW;
+    const int dd0 = threadIdx.y * ND;
+    // First of the 12 staged right values loaded per channel: the value
+    // for (column wl, disparity dd0 + ND - 1) is one after it.
+    const int rs = wl - dd0 + DT - ND;
+
+    float acc[ND][kVecW];
+#pragma unroll
+    for (int i = 0; i < ND; ++i)
+#pragma unroll
+        for (int v = 0; v < kVecW; ++v) acc[i][v] = 0.0f;
+
+    for (int c0 = 0; c0 < Cg; c0 += CC) {
+        const int nc = min(CC, Cg - c0);
+        stage_rows_loop<__half>(Ls, lrow + c0 * plane, plane, nc, w0, tw, W, vec_ok);
+        stage_rows_loop<__half>(Rs, rrow + c0 * plane, plane, nc, w0 - d0 - DT, RW, W, vec_ok);
+        __syncthreads();
+        for (int c = 0; c < nc; ++c) {
+            const uint2 l4 = *reinterpret_cast<const uint2*>(Ls + c * tw + wl);
+            const __half* rp = Rs + c * RW + rs;
+            const uint2 r0 = *reinterpret_cast<const uint2*>(rp);
+            const uint2 r1 = *reinterpret_cast<const uint2*>(rp + 4);
+            const uint2 r2 = *reinterpret_cast<const uint2*>(rp + 8);
+            unsigned short lv[kVecW], rv[12];
+            unpack_h2(l4.x, lv[0], lv[1]);
+            unpack_h2(l4.y, lv[2], lv[3]);
+            unpack_h2(r0.x, rv[0], rv[1]);
+            unpack_h2(r0.y, rv[2], rv[3]);
+            unpack_h2(r1.x, rv[4], rv[5]);
+            unpack_h2(r1.y, rv[6], rv[7]);
+            unpack_h2(r2.x, rv[8], rv[9]);
+            unpack_h2(r2.y, rv[10], rv[11]);
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd)
+#pragma unroll
+                for (int v = 0; v < kVecW; ++v)
+                    acc[dd][v] = fma_h(lv[v], rv[ND - dd + v], acc[dd][v]);
+        }
+        __syncthreads();
+    }
+
+    const float cg = static_cast<float>(Cg);
+    __half* obase = out + (i64(b) * G + g) * i64(D) * plane + i64(h) * W;
+    const int gx = w0 + wl;
+    if (gx >= W) return;
+#pragma unroll
+    for (int dd = 0; dd < ND; ++dd) {
+        const int d = d0 + dd0 + dd;
+        if (d >= D) break;
+        __half* op = obase + i64(d) * plane + gx;
+        __half tmp[kVecW];
+#pragma unroll
+        for (int v = 0; v < kVecW; ++v) {
+            float val;
+            if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
+            else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+            tmp[v] = __float2half_rn(val);
+        }
+        if (gx + kVecW <= W && (reinterpret_cast<uintptr_t>(op) % 8) == 0) {
+            *reinterpret_cast<uint2*>(op) = *reinterpret_cast<uint2*>(tmp);
         } else {
 #pragma unroll
             for (int v = 0; v < kVecW; ++v)
@@ -341,6 +460,28 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             corr_volume_small_kernel<float><<<blocks, 256, 0, stream>>>(
                 static_cast<const float*>(left), static_cast<const float*>(right), static_cast<float*>(out),
                 C, H, W, D, G, total, scale_div, inv_cg);
+        return launch_status("ww_corr_volume");
+    }
+
+    if (is_half && W > 64) {
+        // Column tiles sized to the image: ceil(W / 256) tiles of up to 256
+        // columns, a multiple of 16 (4 columns per thread).
+        const int nt = (W + 255) / 256;
+        const int tw = ((W + nt - 1) / nt + 15) / 16 * 16;
+        const int tx = tw / kVecW;
+        const int ny = max(1, min((D + kDispPerThread - 1) / kDispPerThread, 512 / tx));
+        const int DT = ny * kDispPerThread;
+        const int n_dband = (D + DT - 1) / DT;
+        if (static_cast<long long>(H) * n_dband > 65535) return WW_ERR_UNSUPPORTED;
+        const int cc = kChunkC;
+        const size_t smem = static_cast<size_t>(cc) * (2 * tw + DT) * 2;
+        const int vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
+                           (reinterpret_cast<uintptr_t>(right) % 16 == 0);
+        dim3 block(tx, ny);
+        dim3 grid((W + tw - 1) / tw, H * n_dband, B * G);
+        corr_volume_h_kernel<kChunkC><<<grid, block, smem, stream>>>(
+            static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out), C, H, W,
+            D, G, n_dband, tw, scale_div, inv_cg, vec_ok);
         return launch_status("ww_corr_volume");
     }
 

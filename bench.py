@@ -61,10 +61,15 @@ UNIT = "voxels/s"
 DEFAULT_CONFIG = 4
 
 # DRAM bytes (read + write) per launch of the fused kernel on the full
-# configuration, from ncu captures (profiles/stem_tc_fused_*.md; None until
-# captured).  Config 2: dram__bytes_read.sum 25.24 MB + dram__bytes_write.sum
-# 7.45 MB (most of the output is still in L2 when the launch ends).
-NCU_TRAFFIC_BYTES = {"c2_gwc40_stem32": 32.68e6}
+# configuration, from ncu captures (profiles/stem_tc_fused_*.md).  Configs 2
+# and 5 leave most or all of their output in L2 when the launch ends; config 4
+# is captured at B = 8 and scaled by 64 / 8 (traffic is per pair).
+NCU_TRAFFIC_BYTES = {
+    "c2_gwc40_stem32": 24.84e6 + 7.11e6,
+    "c3_hd_gwc8_stem16": 90.41e6 + 419.93e6,
+    "c4_batched_gwc32_stem32": (274.21e6 + 687.38e6) * 8,
+    "c5_edge_gwc16_stem16": 6.40e6 + 0.001e6,
+}
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per chunk).
 N_E2E_STREAMS = 3
@@ -93,6 +98,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode", "disparity_regression", "stem3_native"],
                     default="corr_cost_stem3d")
+    ap.add_argument("--corr-engine", choices=["tensor", "cuda_cores"], default="tensor",
+                    help="correlation engine of the fused op (ww_set_fused_corr_engine)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
@@ -542,6 +549,8 @@ def bench_main(args, C, cfg, world, rank, local):
     import torch
     import whirlwind_trt_plugins_b200 as ww
     ctx = Ctx(world, rank, local)
+    ww.set_fused_corr_engine(ww.CORR_ENGINE_CUDA_CORES if args.corr_engine == "cuda_cores"
+                             else ww.CORR_ENGINE_TENSOR)
     head = bench_config(args, C, ww, cfg, ctx, steps=args.steps, soak_s=1.5, clocks=True,
                         e2e_steps=max(2, min(args.steps, 5)), cpu_budget_s=10.0)
     if args.profile:
@@ -574,7 +583,7 @@ def bench_main(args, C, cfg, world, rank, local):
         "data": "synthetic (seeded normal/uniform features, N(0,0.05) weights)",
         "config": config_dict(cfg, world), "roofline": head["roofline"], "cpu_baseline": head["cpu_baseline"],
         "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
-        "secondary": secondary,
+        "corr_engine": args.corr_engine, "secondary": secondary,
     }
     print(json.dumps(line), flush=True)
 

@@ -117,14 +117,30 @@ int ww_cost_stem3d(const void* vol, const void* w, const void* b, void* out,
  *   out = ww_cost_stem3d(vol, w, b, act)                          [B, Cout, D, H, W]
  * left, right [B, C, H, W] fp16; w [Cout, G, 3, 3, 3] fp16; b [Cout] fp16.
  * The volume stays in shared memory (fp16, never written to device memory).
- * It is accumulated on the tensor cores in fp32 and scaled by 1/(C/G), so it
- * may differ from ww_corr_volume's in the last fp32 bits (and, after fp16
- * rounding, by one fp16 ulp on rare values); the output agrees with
- * ww_corr_volume followed by ww_cost_stem3d to within 2e-2 absolute.
+ * With the default engine it is accumulated on the tensor cores in fp32 and
+ * scaled by 1/(C/G), so it may differ from ww_corr_volume's in the last fp32
+ * bits (and, after fp16 rounding, by one fp16 ulp on rare values); the
+ * output agrees with ww_corr_volume followed by ww_cost_stem3d to within
+ * 2e-2 absolute.
  * ------------------------------------------------------------------------- */
 int ww_corr_cost_stem3d(const void* left, const void* right, const void* w, const void* b,
                         void* out, int B, int C, int G, int H, int W, int D, int Cout,
                         int act, void* stream);
+
+/* Correlation engine of the fused op (ww_corr_cost_stem3d, _band, _multi),
+ * process-wide; returns the previous engine, or WW_ERR_INVALID_SHAPE for an
+ * unknown value.  Takes effect for launches made after the call.
+ *   WW_CORR_ENGINE_TENSOR      (default) warp-level tensor cores (mma.sync):
+ *                              fp32 accumulation in the tensor core's order.
+ *   WW_CORR_ENGINE_CUDA_CORES  fp32 fma of the fp16 products in channel
+ *                              order: the volume equals ww_corr_volume's bit
+ *                              for bit before the stem.  Measured 1.3x
+ *                              (config 2) to 1.4x (config 4) slower than the
+ *                              tensor engine on a B200. */
+#define WW_CORR_ENGINE_TENSOR 0
+#define WW_CORR_ENGINE_CUDA_CORES 1
+int ww_set_fused_corr_engine(int engine);
+int ww_get_fused_corr_engine(void);
 
 /* Limits of ww_corr_cost_stem3d / _band / _multi and of ww_cost_stem3d
  * (this build): Cout <= 32; D <= 80 when Cout > 16 and D <= 160 when

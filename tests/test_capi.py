@@ -278,3 +278,20 @@ def test_fused_limits_are_reported_and_enforced_at_build_time(ww):
     assert L.ww_plugin_corr_cost_stem3d_output_dims(48, 4, 4, ok, ctypes.byref(out)) == 1   # weights' G != num_groups
     big = descs(desc([1, 64, 20, 40, 96]), desc([32, 64, 3, 3, 3]), desc([32]))
     assert L.ww_plugin_cost_stem3d_output_dims(3, big, ctypes.byref(out)) == 1
+
+
+def test_fused_corr_engine_knob(ww):
+    """The fused op's correlation engine is a process-wide setting: tensor
+    cores by default, CUDA cores on request; unknown values are refused and
+    leave the setting alone."""
+    assert ww.fused_corr_engine() == ww.CORR_ENGINE_TENSOR
+    assert ww.set_fused_corr_engine(ww.CORR_ENGINE_CUDA_CORES) == ww.CORR_ENGINE_TENSOR
+    try:
+        assert ww.fused_corr_engine() == ww.CORR_ENGINE_CUDA_CORES
+        assert ww.lib().ww_set_fused_corr_engine(7) == 2
+        assert ww.fused_corr_engine() == ww.CORR_ENGINE_CUDA_CORES
+        with pytest.raises(ww.WWError):
+            ww.set_fused_corr_engine(-1)
+    finally:
+        assert ww.set_fused_corr_engine(ww.CORR_ENGINE_TENSOR) == ww.CORR_ENGINE_CUDA_CORES
+    assert ww.fused_corr_engine() == ww.CORR_ENGINE_TENSOR

@@ -146,6 +146,60 @@ def test_fused_matches_unfused_composition(ww, torch, orc):
     assert np.array_equal(_u16(vol.cpu().numpy()), _u16(ref_vol))
 
 
+@pytest.fixture
+def cuda_core_engine(ww):
+    prev = ww.set_fused_corr_engine(ww.CORR_ENGINE_CUDA_CORES)
+    yield
+    ww.set_fused_corr_engine(prev)
+
+
+@pytest.mark.parametrize("shape", [
+    # (B, C, G, H, W, D, Cout): Cg = 8, 4, 12, 16 (unrolled channel loops) and
+    # 32, 20, 3, 1 (run-time loop); odd W (scalar staging), D < 8, lone octets
+    (1, 320, 40, 6, 40, 48, 32),
+    (2, 64, 16, 5, 32, 32, 16),
+    (1, 96, 8, 4, 48, 64, 16),
+    (1, 64, 4, 3, 24, 40, 16),
+    (1, 64, 2, 5, 24, 24, 16),
+    (1, 40, 2, 4, 20, 20, 8),
+    (2, 24, 8, 6, 33, 13, 32),
+    (1, 16, 16, 3, 16, 70, 16),
+    (1, 48, 3, 5, 16, 7, 4),
+])
+def test_cuda_core_engine_equals_unfused_composition(ww, torch, cuda_core_engine, shape):
+    """With the CUDA-core correlation engine the fused volume is
+    ww_corr_volume's bit for bit (channel-order fp32 fma chain, the same
+    scale rule), and the stem is the same kernel in both modes, so the fused
+    output equals corr_volume -> cost_stem3d exactly."""
+    from whirlwind_trt_plugins_b200.configs import FrontEnd, make_inputs
+    B, C, G, H, W, D, Cout = shape
+    cfg = FrontEnd("edge", B=B, C=C, G=G, H=H, W=W, D=D, Cout=Cout)
+    x = make_inputs(cfg, seed=C + W + D + 1)
+    tl, tr, tw, tb = (_t(torch, x[k]) for k in ("left", "right", "w", "b"))
+    fused = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+    unfused = ww.cost_stem3d(ww.corr_volume(tl, tr, cfg.D, cfg.G), tw, tb)
+    assert torch.equal(fused, unfused)
+    assert ww.device_error() == 0
+
+
+@pytest.mark.parametrize("cfg_id,B", [(2, 1), (3, 1), (4, 1), (5, 2)])
+def test_cuda_core_engine_full_size(ww, torch, orc, cuda_core_engine, cfg_id, B):
+    """The benchmark configurations at full H x W x D through the CUDA-core
+    engine: bit-identical to the unfused composition and within the fp16
+    tolerance of the oracle."""
+    from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[cfg_id].scaled(B=B)
+    x = make_inputs(cfg)
+    t = {k: _t(torch, x[k]) for k in ("left", "right", "w", "b")}
+    fused = ww.corr_cost_stem3d(t["left"], t["right"], t["w"], t["b"], cfg.D, cfg.G, act=cfg.act)
+    unfused = ww.cost_stem3d(ww.corr_volume(t["left"], t["right"], cfg.D, cfg.G), t["w"], t["b"], act=cfg.act)
+    assert torch.equal(fused, unfused)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, act=cfg.act,
+                        acc_mode=orc.ACC_F32_SEQ).astype(np.float32)
+    assert float(np.abs(fused.cpu().numpy().astype(np.float32) - ref).max()) <= ATOL_F16
+    assert ww.device_error() == 0
+
+
 @pytest.mark.parametrize("shape", [
     # (B, C, G, H, W, D, Cout): channel widths on every correlation path
     (1, 64, 2, 5, 24, 24, 16),     # Cg = 32: channels in two tensor-core chunks

@@ -38,7 +38,8 @@ __all__ = [
     "LIB_PATH", "WWError", "lib", "corr_volume", "cost_stem3d_ref3", "corr_cost_stem3d_ref3", "cost_stem3d",
     "corr_cost_stem3d", "corr_cost_stem3d_band", "nv12_decode", "disparity_regression", "fold_bn", "device_error",
     "clear_device_error", "ACT_RELU", "ACT_RELU6", "DTYPE_FLOAT", "DTYPE_HALF", "DISP_SOFTARGMAX", "DISP_SOFTARGMIN",
-    "MULTI_BATCH", "MULTI_ROWS", "multi_split", "corr_cost_stem3d_multi",
+    "MULTI_BATCH", "MULTI_ROWS", "multi_split", "corr_cost_stem3d_multi", "CORR_ENGINE_TENSOR",
+    "CORR_ENGINE_CUDA_CORES", "set_fused_corr_engine", "fused_corr_engine",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libww_trt_plugins.so")
@@ -51,6 +52,8 @@ DISP_SOFTARGMAX = 0
 DISP_SOFTARGMIN = 1
 MULTI_BATCH = 0
 MULTI_ROWS = 1
+CORR_ENGINE_TENSOR = 0
+CORR_ENGINE_CUDA_CORES = 1
 
 STATUS = {
     0: "success", 1: "CUDA launch or runtime call failed", 2: "invalid tensor shape",
@@ -89,6 +92,8 @@ def _load() -> ctypes.CDLL:
     L.ww_multi_inject_copy_failure.argtypes = [i]
     L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.ww_clear_device_error.argtypes = []
+    L.ww_set_fused_corr_engine.argtypes = [i]
+    L.ww_get_fused_corr_engine.argtypes = []
     del f
     return L
 
@@ -402,6 +407,20 @@ def fold_bn(w, scale, bias):
     _check("ww_fold_bn_f16", _lib.ww_fold_bn_f16(w.ctypes.data, scale.ctypes.data, bias.ctypes.data, cout, k,
                                                  w16.ctypes.data, b16.ctypes.data))
     return w16.view(np.float16), b16.view(np.float16)
+
+
+def set_fused_corr_engine(engine: int) -> int:
+    """Select the fused op's correlation engine (CORR_ENGINE_TENSOR, the
+    default, or CORR_ENGINE_CUDA_CORES: a channel-order fp32 fma chain whose
+    volume equals corr_volume's bit for bit); returns the previous one."""
+    prev = _lib.ww_set_fused_corr_engine(int(engine))
+    if engine not in (CORR_ENGINE_TENSOR, CORR_ENGINE_CUDA_CORES):
+        _check("ww_set_fused_corr_engine", prev)
+    return prev
+
+
+def fused_corr_engine() -> int:
+    return _lib.ww_get_fused_corr_engine()
 
 
 def device_error() -> int:

@@ -19,6 +19,8 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                    int act, int in_row0, int in_rows, int out_row0, int out_rows,
                    cudaStream_t stream) noexcept;
 int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept;
+int set_fused_corr_engine(int engine) noexcept;
+int fused_corr_engine() noexcept;
 int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT,
                        int W_OUT, cudaStream_t stream) noexcept;
 int disparity_regression_launch(const void* cost, void* out, int in_dtype, int out_dtype, int B, int D, int H,
@@ -113,6 +115,16 @@ static int smem_optin_or_b200() noexcept
     if (ww::current_device_info(&d) == WW_SUCCESS) return d.smem_optin;
     cudaGetLastError();
     return 232448;
+}
+
+int ww_set_fused_corr_engine(int engine)
+{
+    return ww::set_fused_corr_engine(engine);
+}
+
+int ww_get_fused_corr_engine(void)
+{
+    return ww::fused_corr_engine();
 }
 
 int ww_corr_cost_stem3d_supported(int C, int G, int D, int Cout)

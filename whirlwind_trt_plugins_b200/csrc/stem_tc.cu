@@ -70,6 +70,7 @@
 #include "ww_common.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 namespace ww {
@@ -93,6 +94,7 @@ constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
 constexpr int kMaxVBuf = 3;        // volume row buffers
+constexpr int kMaxFItems = 10 * 24;  // CUDA-core correlation items per job (10 columns x ceil(D/8) + 2 tiles)
 // M-blocks the epilogue drains (tensor memory -> registers, slot released)
 // before it stores any of them.  The MMA warp needs every M-block's slot
 // back before the first K-step of the next row, so a row with more M-blocks
@@ -123,6 +125,9 @@ struct StemParams {
     int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
     int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
     int n_rbox;               // right boxes of 64 columns per job
+    int scale_div;            // CUDA-core correlation: 1 = sum / Cg (rounded division), 0 = sum * (1 / Cg)
+    int n_fitems;             // CUDA-core correlation: items per job (see corr_item_fma)
+    int fma_span;             // CUDA-core correlation: most jobs one producer task touches
     uint32_t tmem_cols;
     uint32_t off_b, off_vol, vol_buf_bytes, lbo_vol, off_stage, stage_slot_bytes, off_bar;
     uint32_t rbox_bytes;      // one right box: 8 Cg rows x 128 bytes
@@ -139,6 +144,10 @@ struct StemParams {
     // of real groups in the octet.
     int step_off[2 * kMaxSteps];
     int step_gv[2 * kMaxSteps];
+    // CUDA-core correlation items of a job, ordered by (right tile, volume
+    // column): bits 0..3 volume column w', 4..9 right tile jt, 15 set when
+    // all 8 disparities of the item lie in [0, D).
+    uint16_t fitems[kMaxFItems];
     // TMA maps of the left / right features (4-D: x = W, y = row, z = channel,
     // w = batch); boxes [24] x [8 Cg] (left) and [64] x [8 Cg] (right, swizzled).
     CUtensorMap tmap_l;
@@ -523,9 +532,83 @@ __device__ __forceinline__ void issue_row_n(const StemParams& p, uint32_t tmem_b
     }
 }
 
+// Group-wise correlation of one item of a staging job on the CUDA cores:
+// item (volume column w', right tile jt, group half q) is, for the groups
+// e = 4q .. 4q+3 of the octet, the 8 disparities d = 8 ceil(D/8) - 1 + w' - x'
+// of the staged right columns x' = 8 jt .. 8 jt + 7:
+//     vol[e][d][w'] = round_fp16(scale(sum_c L[e Cg + c][w'] * R[e Cg + c][x']))
+// summed as one fp32 fma chain in channel order, c = 0 .. Cg-1, from +0 (the
+// fp16 products are exact in fp32) and scaled as ww_corr_volume scales the
+// same call (scale_div: / Cg, else * (1 / Cg)): the same value, bit for bit,
+// as ww_corr_volume's.  Per (channel, group) a lane reads one
+// 16-byte chunk of right columns and one left value and does 8 fmas into
+// acc[group][x' - 8 jt]; the 4 groups of a disparity are then one 8-byte
+// half of a 16-byte volume row.  The lanes of a quarter warp take
+// consecutive columns w' of one tile, so their right reads are one
+// broadcast and their volume rows (11 rows apart between neighbouring w' at
+// equal x') fall in distinct bank groups.  CG > 0: Cg known at compile time.
+template <int CG>
+__device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t* stage, uint8_t* vol, int item,
+                                              int q)
+{
+    const int ent = p.fitems[item];
+    const int wp = ent & 15, jt = (ent >> 4) & 63;
+    const bool full = (ent & 0x8000) != 0;
+    const int Cg = CG > 0 ? CG : p.Cg;
+    // Right chunk of staged columns [8 jt, 8 jt + 8) in row r: box jt / 8,
+    // 16-byte chunk (jt % 8) ^ (r % 8) of the row (128-byte TMA swizzle).
+    const uint8_t* rbox = stage + (jt >> 3) * p.rbox_bytes + 4 * q * Cg * 128;
+    const uint32_t jsw = static_cast<uint32_t>(jt & 7);
+    const uint8_t* lcol = stage + p.off_l + 2 * (wp + 7) + 4 * q * Cg * kLRowBytes;  // staged column w' + 7
+    const int rq = 4 * q * Cg;  // first row of the half
+    float acc[4][8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[e][j] = 0.0f;
+#pragma unroll(CG > 0 ? CG : 1)
+    for (int c = 0; c < Cg; ++c) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int rl = e * Cg + c;  // row within the half
+            const uint32_t sw = ((jsw ^ static_cast<uint32_t>((rq + rl) & 7)) << 4);
+            const uint4 rv = *reinterpret_cast<const uint4*>(rbox + rl * 128 + sw);
+            const unsigned short lv = *reinterpret_cast<const unsigned short*>(lcol + rl * kLRowBytes);
+            unsigned short h[8];
+            unpack_b16x2(rv.x, h[0], h[1]);
+            unpack_b16x2(rv.y, h[2], h[3]);
+            unpack_b16x2(rv.z, h[4], h[5]);
+            unpack_b16x2(rv.w, h[6], h[7]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[e][j] = fma_f16f16f32(lv, h[j], acc[e][j]);
+        }
+    }
+    const int d0 = 8 * (p.n_tiles - 2) - 1 + wp - 8 * jt;  // disparity of x' = 8 jt
+    uint8_t* row0 = vol + ((d0 + 1) * kWtp + wp) * 16 + 8 * q;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = d0 - j;
+        if (full || (d >= 0 && d < p.D)) {
+            uint2 v;
+            if (p.scale_div) {
+                const float cg = static_cast<float>(Cg);
+                const __half2 h01 = __floats2half2_rn(__fdiv_rn(acc[0][j], cg), __fdiv_rn(acc[1][j], cg));
+                const __half2 h23 = __floats2half2_rn(__fdiv_rn(acc[2][j], cg), __fdiv_rn(acc[3][j], cg));
+                v.x = *reinterpret_cast<const uint32_t*>(&h01);
+                v.y = *reinterpret_cast<const uint32_t*>(&h23);
+            } else {
+                v.x = scale_to_half2(acc[0][j], acc[1][j], p.inv_cg);
+                v.y = scale_to_half2(acc[2][j], acc[3][j], p.inv_cg);
+            }
+            *reinterpret_cast<uint2*>(row0 - j * kWtp * 16) = v;
+        }
+    }
+}
+
 // Correlation variants (a kernel template parameter, so each instantiation
-// carries only its own producer path): 1: Cg == 8, 2: Cg < 8, 3: Cg == 16,
-// 4: 8 < Cg < 16, 5: Cg > 16.
+// carries only its own producer path).  Warp-level tensor cores: 1: Cg == 8,
+// 2: Cg < 8, 3: Cg == 16, 4: 8 < Cg < 16, 5: Cg > 16.  CUDA cores
+// (corr_item_fma): 6: Cg == 8, 7: Cg == 4, 8: Cg == 12, 9: Cg == 16, 10: any.
 template <int CORR>
 __device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, uint32_t zero_row, uint32_t vsa,
                                           int jt0, int jt1, int lane)
@@ -537,8 +620,22 @@ __device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, ui
     else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane);
 }
 
-inline int corr_variant(int Cg)
+template <int CORR>
+__device__ __forceinline__ void corr_item(const StemParams& p, const uint8_t* stage, uint8_t* vol, int item, int q)
 {
+    if constexpr (CORR == 6) corr_item_fma<8>(p, stage, vol, item, q);
+    else if constexpr (CORR == 7) corr_item_fma<4>(p, stage, vol, item, q);
+    else if constexpr (CORR == 8) corr_item_fma<12>(p, stage, vol, item, q);
+    else if constexpr (CORR == 9) corr_item_fma<16>(p, stage, vol, item, q);
+    else corr_item_fma<0>(p, stage, vol, item, q);
+}
+
+// Correlation engine of the fused kernel (WW_CORR_ENGINE_*), process-wide.
+std::atomic<int> g_corr_engine{WW_CORR_ENGINE_TENSOR};
+
+inline int corr_variant(int Cg, bool cuda_cores)
+{
+    if (cuda_cores) return Cg == 8 ? 6 : Cg == 4 ? 7 : Cg == 12 ? 8 : Cg == 16 ? 9 : 10;
     return Cg == 8 ? 1 : Cg < 8 ? 2 : Cg == 16 ? 3 : Cg < 16 ? 4 : 5;
 }
 
@@ -972,7 +1069,52 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             if (it >= NV && !warp_wait(smem_addr(&vol_empty[vb]), ((it / NV) - 1) & 1, p.err, 4)) break;
             if (u >= 0 && u < p.H) {
                 uint8_t* vbuf = sVol + vb * p.vol_buf_bytes;
-                if (FUSED) {
+                if (FUSED && CORR >= 6) {
+                    // CUDA-core correlation: the row's KG * n_fitems items
+                    // (job-major) in tasks of 32; task tau of the row goes to
+                    // warp (it * n_tasks + tau) mod kProdWarps.  A warp waits
+                    // for every job up to the last one its next task touches
+                    // and releases every job before that task's first one
+                    // (a task spans at most fma_span <= n_slots jobs), and
+                    // every warp waits for and releases all KG jobs in order.
+                    const int job0 = (u - uv0) * p.KG;
+                    const int P = 2 * p.n_fitems;  // (group half, table entry) items per job
+                    const int n_items = p.KG * P;
+                    const int n_tasks = (n_items + 31) / 32;
+                    int waited = 0, released = 0;
+                    for (int tau = ((pw - it * n_tasks) % kProdWarps + kProdWarps) % kProdWarps; tau < n_tasks && ok;
+                         tau += kProdWarps) {
+                        const int i0 = tau * 32;
+                        const int kg_first = i0 / P, kg_last = (min(i0 + 32, n_items) - 1) / P;
+                        for (; released < kg_first; ++released) {
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(smem_addr(&stage_empty[(job0 + released) % p.n_slots]));
+                        }
+                        for (; waited <= kg_last && ok; ++waited) {
+                            const int job = job0 + waited;
+                            ok = warp_wait(smem_addr(&stage_full[job % p.n_slots]), (job / p.n_slots) & 1, p.err, 7);
+                        }
+                        if (!ok) break;
+                        const int item = i0 + lane;
+                        if (item < n_items) {
+                            const int kg = item / P;
+                            const int job = job0 + kg;
+                            const int k = item - kg * P;
+                            const int q = k >= p.n_fitems ? 1 : 0;
+                            corr_item<CORR>(p, smem + p.off_stage + (job % p.n_slots) * p.stage_slot_bytes,
+                                            vbuf + kg * p.lbo_vol, k - q * p.n_fitems, q);
+                        }
+                    }
+                    for (; waited < p.KG && ok; ++waited) {
+                        const int job = job0 + waited;
+                        ok = warp_wait(smem_addr(&stage_full[job % p.n_slots]), (job / p.n_slots) & 1, p.err, 7);
+                    }
+                    if (ok) {
+                        __syncwarp();
+                        for (; released < p.KG; ++released)
+                            if (lane == 0) mbar_arrive(smem_addr(&stage_empty[(job0 + released) % p.n_slots]));
+                    }
+                } else if (FUSED) {
                     const int job0 = (u - uv0) * p.KG;  // job of (u, octet 0)
                     for (int kg = 0; kg < p.KG && ok; ++kg) {
                         const int job = job0 + kg;
@@ -1035,26 +1177,33 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     if (warp == kMmaWarp) tmem_dealloc(tmem_base, p.tmem_cols);
 }
 
-// Raise a kernel's dynamic shared-memory limit to the device's opt-in maximum
-// once per (kernel, device) instead of on every launch: the attribute is a
-// driver call, and launches with any smaller size then need nothing.
-bool ensure_smem_limit(const void* kernel, int device, int optin) noexcept
+// CTAs of `kernel` resident per SM with `smem` bytes of dynamic shared
+// memory (registers, threads and shared memory; 0 = a CUDA call failed).
+// The first call for a (kernel, device) raises the kernel's dynamic
+// shared-memory limit to the device's opt-in maximum, so launches with any
+// smaller size need nothing more; both driver queries are cached per
+// (kernel, device, smem) instead of running on every launch.
+int resident_ctas(const void* kernel, int device, int optin, size_t smem) noexcept
 {
     constexpr int kSlots = 64;
+    struct Entry { const void* fn; int dev; size_t smem; int ctas; };
     static std::mutex mu;
-    static const void* done_fn[kSlots];
-    static int done_dev[kSlots];
+    static Entry done[kSlots];
     static int n_done = 0;
     std::lock_guard<std::mutex> lock(mu);
-    for (int i = 0; i < n_done; ++i)
-        if (done_fn[i] == kernel && done_dev[i] == device) return true;
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) return false;
-    if (n_done < kSlots) {
-        done_fn[n_done] = kernel;
-        done_dev[n_done] = device;
-        ++n_done;
+    bool raised = false;
+    for (int i = 0; i < n_done; ++i) {
+        if (done[i].fn != kernel || done[i].dev != device) continue;
+        raised = true;
+        if (done[i].smem == smem) return done[i].ctas;
     }
-    return true;
+    if (!raised && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+        return 0;
+    int ctas = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, kernel, kThreads, smem) != cudaSuccess || ctas < 1)
+        return 0;
+    if (n_done < kSlots) done[n_done++] = Entry{kernel, device, smem, ctas};
+    return ctas;
 }
 
 uint32_t pow2_cols(uint32_t c)
@@ -1065,6 +1214,19 @@ uint32_t pow2_cols(uint32_t c)
 }
 
 }  // namespace
+
+int corr_scale_div_grouped(bool is_half, int B, int C, int G, int H, int W, int D, int sm_count) noexcept;
+
+int set_fused_corr_engine(int engine) noexcept
+{
+    if (engine != WW_CORR_ENGINE_TENSOR && engine != WW_CORR_ENGINE_CUDA_CORES) return WW_ERR_INVALID_SHAPE;
+    return g_corr_engine.exchange(engine);
+}
+
+int fused_corr_engine() noexcept
+{
+    return g_corr_engine.load();
+}
 
 // Whether the stem kernel takes a shape: WW_SUCCESS, WW_ERR_INVALID_SHAPE or
 // WW_ERR_UNSUPPORTED (the limits of this build: Cout <= 32; the stem's
@@ -1211,6 +1373,30 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     // (and so the staging ring's turnover) short (measured: 7 % faster than
     // one tile per task on config 2, and faster on every config).
     p.tpj = (p.n_tiles + 1) / 2;
+    // CUDA-core correlation items: (right tile, volume column) pairs with
+    // any disparity in [0, D), and the most jobs a task of 32 items touches.
+    const bool cuda_core_corr = fused && g_corr_engine.load(std::memory_order_relaxed) == WW_CORR_ENGINE_CUDA_CORES;
+    p.n_fitems = 0;
+    p.fma_span = 0;
+    p.scale_div = 0;
+    if (cuda_core_corr) {
+        // (* 1 / Cg is exactly / Cg when Cg is a power of two)
+        p.scale_div = (Cg & (Cg - 1)) == 0 ? 0 : corr_scale_div_grouped(true, B, C, G, H, W, D, dev.sm_count);
+        const int dbase = 8 * (p.n_tiles - 2) - 1;
+        for (int jt = 0; jt < p.n_tiles; ++jt)
+            for (int wp = 0; wp < kWtp; ++wp) {
+                const int dmax = dbase + wp - 8 * jt, dmin = dmax - 7;
+                if (dmax < 0 || dmin > D - 1) continue;
+                if (p.n_fitems >= kMaxFItems) return WW_ERR_UNSUPPORTED;
+                const bool full = dmin >= 0 && dmax <= D - 1;
+                p.fitems[p.n_fitems++] = static_cast<uint16_t>(wp | (jt << 4) | (full ? 0x8000 : 0));
+            }
+        const int per_job = 2 * p.n_fitems;  // two group halves per entry
+        const int n_items = KG * per_job;
+        for (int i0 = 0; i0 < n_items; i0 += 32)
+            p.fma_span = std::max(p.fma_span, (std::min(i0 + 32, n_items) - 1) / per_job - i0 / per_job + 1);
+        if (p.fma_span > p.n_slots) return WW_ERR_UNSUPPORTED;
+    }
     p.out_vec = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     {
         const size_t wbytes = static_cast<size_t>(Cout) * G * 54;
@@ -1240,10 +1426,33 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
         p.tmplB[s] = host_smem_desc(static_cast<uint32_t>(s * 2 * 5 * coutp * 16), 5 * coutp * 16, 128);
     }
 
-    // Strip length: minimise (waves of CTAs) x (rows streamed per CTA).
+    using KernelFn = void (*)(StemParams);
+    KernelFn kernel = nullptr;
+    if (!fused) {
+        kernel = coutp == 16 ? stem_tc_kernel<16, false, 0> : stem_tc_kernel<32, false, 0>;
+    } else {
+        const int cv = corr_variant(Cg, cuda_core_corr);
+#define WW_FUSED_CASE(CP, CV) \
+    if (coutp == CP && cv == CV) kernel = stem_tc_kernel<CP, true, CV>;
+        WW_FUSED_CASE(16, 1) WW_FUSED_CASE(16, 2) WW_FUSED_CASE(16, 3) WW_FUSED_CASE(16, 4) WW_FUSED_CASE(16, 5)
+        WW_FUSED_CASE(32, 1) WW_FUSED_CASE(32, 2) WW_FUSED_CASE(32, 3) WW_FUSED_CASE(32, 4) WW_FUSED_CASE(32, 5)
+        WW_FUSED_CASE(16, 6) WW_FUSED_CASE(16, 7) WW_FUSED_CASE(16, 8) WW_FUSED_CASE(16, 9) WW_FUSED_CASE(16, 10)
+        WW_FUSED_CASE(32, 6) WW_FUSED_CASE(32, 7) WW_FUSED_CASE(32, 8) WW_FUSED_CASE(32, 9) WW_FUSED_CASE(32, 10)
+#undef WW_FUSED_CASE
+    }
+    if (kernel == nullptr) return WW_ERR_UNSUPPORTED;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return WW_ERR_DEVICE;
+    const char* op = fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d";
+    const int resident = resident_ctas(reinterpret_cast<const void*>(kernel), device, dev.smem_optin, smem);
+    if (resident == 0) return launch_status(op);
+
+    // Strip length: minimise (waves of CTAs) x (rows streamed per CTA), with
+    // the CTAs an SM holds at once limited by registers, shared memory and
+    // the tensor-memory columns each CTA allocates (at 448 threads and
+    // 120-128 registers a thread the fused kernel runs one CTA per SM).
     const long long col_tiles = static_cast<long long>(B) * p.n_wtiles;
-    const int ctas_per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(
-        dev.smem_optin / (smem + 1024), 512 / p.tmem_cols)));
+    const int ctas_per_sm = std::max(1, std::min(resident, static_cast<int>(512 / p.tmem_cols)));
     const long long slots = static_cast<long long>(dev.sm_count) * ctas_per_sm;
     int best_s = out_rows;
     long long best_cost = -1;
@@ -1257,23 +1466,8 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.n_strips = (out_rows + best_s - 1) / best_s;
     const long long grid = col_tiles * p.n_strips;
     if (grid > 0x7fffffffLL) return WW_ERR_UNSUPPORTED;
-
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess) return WW_ERR_DEVICE;
-    auto launch = [&](auto kernel) -> int {
-        if (!ensure_smem_limit(reinterpret_cast<const void*>(kernel), device, dev.smem_optin))
-            return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
-        kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
-        return launch_status(fused ? "ww_corr_cost_stem3d" : "ww_cost_stem3d");
-    };
-    if (!fused) return coutp == 16 ? launch(stem_tc_kernel<16, false, 0>) : launch(stem_tc_kernel<32, false, 0>);
-    const int cv = corr_variant(Cg);
-#define WW_FUSED_CASE(CP, CV) \
-    if (coutp == CP && cv == CV) return launch(stem_tc_kernel<CP, true, CV>);
-    WW_FUSED_CASE(16, 1) WW_FUSED_CASE(16, 2) WW_FUSED_CASE(16, 3) WW_FUSED_CASE(16, 4) WW_FUSED_CASE(16, 5)
-    WW_FUSED_CASE(32, 1) WW_FUSED_CASE(32, 2) WW_FUSED_CASE(32, 3) WW_FUSED_CASE(32, 4) WW_FUSED_CASE(32, 5)
-#undef WW_FUSED_CASE
-    return WW_ERR_UNSUPPORTED;
+    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
+    return launch_status(op);
 }
 
 }  // namespace ww

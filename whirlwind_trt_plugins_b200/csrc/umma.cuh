@@ -346,6 +346,11 @@ __device__ __forceinline__ uint32_t pack_b16x2(unsigned short lo, unsigned short
     return r;
 }
 
+__device__ __forceinline__ void unpack_b16x2(uint32_t v, unsigned short& lo, unsigned short& hi)
+{
+    asm("mov.b32 {%0, %1}, %2;\n" : "=h"(lo), "=h"(hi) : "r"(v));
+}
+
 __device__ __forceinline__ void st_shared_u16(uint32_t saddr, unsigned short v)
 {
     asm volatile("st.shared.u16 [%0], %1;\n" : : "r"(saddr), "h"(v) : "memory");

@@ -339,6 +339,173 @@ __global__ void __launch_bounds__(512) corr_volume_h_kernel(
     }
 }
 
+// cp.async staging of rows [0, nc) x columns [col0, col0 + width) of one
+// image row into dst[nc][width] (16-byte vectors; W % 8 == 0 and 16-byte
+// aligned bases, so a vector is wholly inside or wholly outside the image;
+// outside ones are zero-filled by the copy itself).  Not waited for here.
+__device__ __forceinline__ void stage_rows_async(__half* dst, const __half* src_row0, int64_t chan_stride, int nc,
+                                                 int col0, int width, int W)
+{
+    const int nvec = width / 8;
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < nc * nvec; i += blockDim.x * blockDim.y) {
+        const int c = i / nvec;
+        const int x = (i - c * nvec) * 8;
+        const int gx = col0 + x;
+        const bool in = gx >= 0 && gx < W;
+        const __half* src = src_row0 + c * chan_stride + (in ? gx : 0);
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + c * width + x));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" : : "r"(d), "l"(src), "r"(in ? 16 : 0)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+// (x * s, y * s) with one packed fp32 multiply (each lane rounded as
+// __fmul_rn) and one packed round to fp16 (each as __float2half_rn).
+__device__ __forceinline__ uint32_t scale2_to_half2(float x, float y, float s)
+{
+    uint64_t v, sv, r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(x), "f"(y));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(sv) : "f"(s));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(v), "l"(sv));
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+    const __half2 h2 = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h2);
+}
+
+// fp16, W > 64, W % 8 == 0, the group's channels in one staged chunk
+// (Cg <= CC) and all disparities in one band.  The register tile and the
+// arithmetic are corr_volume_h_kernel's (4 columns x 8 disparities per
+// thread, fp32 fma chains in channel order from +0, the same scale rule and
+// rounding), so the results are bit-identical.  Two changes:
+//   * a CTA streams `rows` consecutive image rows of one (b, g, column
+//     tile) through a ring of three row buffers: row h + 2's left and right
+//     segments are copied in (cp.async, zero fill off the image) while row h
+//     is computed and stored, so only the first row waits for its copy, one
+//     barrier per row suffices, and the grid is about one wave of resident
+//     CTAs;
+//   * the epilogue costs about 1.5 instructions per output instead of 4 for
+//     threads whose 8 disparities are all <= their first column (no w - d < 0
+//     test; scale and fp16 rounding packed two values at a time): with Cg = 8
+//     a value takes only 8 fmas, so the epilogue was most of the
+//     instructions (measured).
+// Measured alternatives that were slower: fp32 copies of the staged rows
+// (one conversion per staged value instead of per use: more registers,
+// fewer CTAs), bulk-copy (TMA engine) staging of the 2 Cg row segments
+// from one thread, and selecting the w - d < 0 zeros before a shared
+// packed epilogue.
+// CG: channels per group when known at compile time (the channel loop is
+// then unrolled with immediate offsets), 0 otherwise.  64 registers: 4 CTAs
+// of 240 threads per SM (measured faster than 80 registers and 3 CTAs on
+// every benchmark shape but config 2, where it is 4 % slower).
+template <int CC, int CG>
+__global__ void __maxnreg__(64) corr_volume_rows_kernel(
+    const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
+    int C, int H, int W, int D, int G, int rows, int tw, int scale_div, float inv_cg)
+{
+    constexpr int ND = kDispPerThread;
+    const int DT = ND * blockDim.y;
+    const int RW = tw + DT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half* buf = reinterpret_cast<__half*>(smem_raw);
+    const int buf_elems = CC * (tw + RW);
+
+    const int w0 = blockIdx.x * tw;
+    const int h0 = blockIdx.y * rows;
+    const int h1 = min(h0 + rows, H);
+    const int b = blockIdx.z / G;
+    const int g = blockIdx.z - b * G;
+    const int Cg = CG > 0 ? CG : C / G;
+    const int64_t plane = i64(H) * W;
+    const __half* lbase = left + (i64(b) * C + i64(g) * Cg) * plane;
+    const __half* rbase = right + (i64(b) * C + i64(g) * Cg) * plane;
+
+    const int wl = threadIdx.x * kVecW;
+    const int dd0 = threadIdx.y * ND;
+    const int rs = wl - dd0 + DT - ND;
+    const int gx = w0 + wl;
+    // Every output of this thread has w >= d (no zero fill), all 8
+    // disparities exist, and all 4 columns are inside the image.
+    const bool plain = gx >= dd0 + ND - 1 && dd0 + ND <= D && gx + kVecW <= W && !scale_div;
+    __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
+
+    auto stage = [&](int hh) {
+        __half* nL = buf + ((hh - h0) % 3) * buf_elems;
+        stage_rows_async(nL, lbase + i64(hh) * W, plane, Cg, w0, tw, W);
+        stage_rows_async(nL + CC * tw, rbase + i64(hh) * W, plane, Cg, w0 - DT, RW, W);
+    };
+    if (h0 < h1) stage(h0);
+    if (h0 + 1 < h1) stage(h0 + 1);
+    for (int h = h0; h < h1; ++h) {
+        const __half* Ls = buf + ((h - h0) % 3) * buf_elems;
+        const __half* Rs = Ls + CC * tw;
+        if (h + 1 < h1) asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+        else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();  // row h landed for every thread; row h - 1's compute done everywhere
+        if (h + 2 < h1) stage(h + 2);  // into row h - 1's buffer
+        float acc[ND][kVecW];
+#pragma unroll
+        for (int i = 0; i < ND; ++i)
+#pragma unroll
+            for (int v = 0; v < kVecW; ++v) acc[i][v] = 0.0f;
+#pragma unroll(CG > 0 ? CG : 1)
+        for (int c = 0; c < Cg; ++c) {
+            const uint2 l4 = *reinterpret_cast<const uint2*>(Ls + c * tw + wl);
+            const __half* rp = Rs + c * RW + rs;
+            const uint2 r0 = *reinterpret_cast<const uint2*>(rp);
+            const uint2 r1 = *reinterpret_cast<const uint2*>(rp + 4);
+            const uint2 r2 = *reinterpret_cast<const uint2*>(rp + 8);
+            unsigned short lv[kVecW], rv[12];
+            unpack_h2(l4.x, lv[0], lv[1]);
+            unpack_h2(l4.y, lv[2], lv[3]);
+            unpack_h2(r0.x, rv[0], rv[1]);
+            unpack_h2(r0.y, rv[2], rv[3]);
+            unpack_h2(r1.x, rv[4], rv[5]);
+            unpack_h2(r1.y, rv[6], rv[7]);
+            unpack_h2(r2.x, rv[8], rv[9]);
+            unpack_h2(r2.y, rv[10], rv[11]);
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd)
+#pragma unroll
+                for (int v = 0; v < kVecW; ++v) acc[dd][v] = fma_h(lv[v], rv[ND - dd + v], acc[dd][v]);
+        }
+        __half* op = obase + i64(h) * W;
+        if (plain) {
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd) {
+                uint2 u;
+                u.x = scale2_to_half2(acc[dd][0], acc[dd][1], inv_cg);
+                u.y = scale2_to_half2(acc[dd][2], acc[dd][3], inv_cg);
+                *reinterpret_cast<uint2*>(op + dd * plane) = u;
+            }
+        } else if (gx < W) {
+            const float cg = static_cast<float>(Cg);
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd) {
+                const int d = dd0 + dd;
+                if (d >= D) break;
+                __half tmp[kVecW];
+#pragma unroll
+                for (int v = 0; v < kVecW; ++v) {
+                    float val;
+                    if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
+                    else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    tmp[v] = __float2half_rn(val);
+                }
+                __half* o = op + dd * plane;
+                if (gx + kVecW <= W) {
+                    *reinterpret_cast<uint2*>(o) = *reinterpret_cast<uint2*>(tmp);
+                } else {
+#pragma unroll
+                    for (int v = 0; v < kVecW; ++v)
+                        if (gx + v < W) o[v] = tmp[v];
+                }
+            }
+        }
+    }
+}
+
 // Small volumes (fewer than kSmallOutputsPerSM outputs per SM; the
 // reference's native 1 x 48 x 32 x 40 is one): one thread per output, both
 // operands read straight through L2, the channel loop unrolled so 8 channels'
@@ -477,6 +644,38 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
         const size_t smem = static_cast<size_t>(cc) * (2 * tw + DT) * 2;
         const int vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
                            (reinterpret_cast<uintptr_t>(right) % 16 == 0);
+        if (vec_ok && n_dband == 1 && Cg <= cc) {
+            // Row-streaming form (two staged rows in shared memory): rows
+            // per CTA chosen to minimise (waves of resident CTAs) x (rows
+            // per CTA + 1 for the first row's copy).
+            const size_t rsmem = 3 * smem;  // three staged rows
+            using RowsFn = void (*)(const __half*, const __half*, __half*, int, int, int, int, int, int, int, int,
+                                    float);
+            RowsFn kern = Cg == 4    ? corr_volume_rows_kernel<kChunkC, 4>
+                          : Cg == 8  ? corr_volume_rows_kernel<kChunkC, 8>
+                          : Cg == 12 ? corr_volume_rows_kernel<kChunkC, 12>
+                          : Cg == 16 ? corr_volume_rows_kernel<kChunkC, 16>
+                                     : corr_volume_rows_kernel<kChunkC, 0>;
+            int resident = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, tx * ny, rsmem) != cudaSuccess ||
+                resident < 1)
+                return launch_status("ww_corr_volume");
+            const long long slots = static_cast<long long>(resident) * dev.sm_count;
+            const long long tiles = static_cast<long long>(nt) * B * G;
+            int best = H;
+            long long best_cost = -1;
+            for (int r = 1; r <= H; ++r) {
+                const long long ctas = tiles * ((H + r - 1) / r);
+                const long long cost = ((ctas + slots - 1) / slots) * (r + 1);
+                if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = r; }
+            }
+            dim3 block(tx, ny);
+            dim3 grid(nt, (H + best - 1) / best, B * G);
+            kern<<<grid, block, rsmem, stream>>>(
+                static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out), C,
+                H, W, D, G, best, tw, scale_div, inv_cg);
+            return launch_status("ww_corr_volume");
+        }
         dim3 block(tx, ny);
         dim3 grid((W + tw - 1) / tw, H * n_dband, B * G);
         corr_volume_h_kernel<kChunkC><<<grid, block, smem, stream>>>(

@@ -76,6 +76,7 @@ def _ref_available():
     (1, 16, 32, 128, 48, 1), (1, 12, 32, 128, 48, 1), (2, 64, 16, 80, 24, 1), (1, 24, 12, 64, 64, 2),
     (1, 320, 16, 160, 48, 40), (2, 64, 12, 128, 32, 16), (1, 32, 7, 40, 30, 4), (1, 8, 3, 200, 36, 1),
     (2, 32, 96, 48, 64, 1), (2, 16, 128, 24, 32, 2),
+    (1, 64, 6, 312, 48, 8), (1, 96, 5, 320, 64, 8),  # row-streaming kernels over two column tiles
 ])
 def test_corr_matches_reference_live(ww, torch, orc, shape):
     if not _ref_available():
@@ -94,7 +95,7 @@ def test_corr_matches_reference_live(ww, torch, orc, shape):
     assert np.array_equal(_bits(out).reshape(-1), _bits(ref.cpu().numpy()).reshape(-1))
 
 
-@pytest.mark.parametrize("cfg_id", [1, 2, 3, 5])
+@pytest.mark.parametrize("cfg_id", [1, 2, 3, 4, 5])
 def test_corr_configs_match_oracle(ww, torch, orc, cfg_id):
     from whirlwind_trt_plugins_b200.configs import CONFIGS, make_inputs
     cfg = CONFIGS[cfg_id]

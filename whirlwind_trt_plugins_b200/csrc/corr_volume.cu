@@ -506,6 +506,124 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
     }
 }
 
+// The same row streaming with an 8-column x 8-disparity register tile per
+// thread (corr_volume_rows_kernel's is 4 x 8): per channel one 16-byte left
+// load and two 16-byte right loads feed 64 fmas, and the epilogue stores 16
+// bytes per disparity, so loads, epilogue and per-row overhead per output
+// are about half.  Same arithmetic, so bit-identical results.  blockDim =
+// (tw / 8, ny), DT = 8 ny.
+template <int CC, int CG>
+__global__ void __maxnreg__(128) corr_volume_rows8_kernel(
+    const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
+    int C, int H, int W, int D, int G, int rows, int tw, int scale_div, float inv_cg)
+{
+    constexpr int ND = kDispPerThread;
+    constexpr int VW = 8;
+    const int DT = ND * blockDim.y;
+    const int RW = tw + DT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half* buf = reinterpret_cast<__half*>(smem_raw);
+    const int buf_elems = CC * (tw + RW);
+
+    const int w0 = blockIdx.x * tw;
+    const int h0 = blockIdx.y * rows;
+    const int h1 = min(h0 + rows, H);
+    const int b = blockIdx.z / G;
+    const int g = blockIdx.z - b * G;
+    const int Cg = CG > 0 ? CG : C / G;
+    const int64_t plane = i64(H) * W;
+    const __half* lbase = left + (i64(b) * C + i64(g) * Cg) * plane;
+    const __half* rbase = right + (i64(b) * C + i64(g) * Cg) * plane;
+
+    const int wl = threadIdx.x * VW;
+    const int dd0 = threadIdx.y * ND;
+    const int rs = wl - dd0 - ND + DT;  // 8-aligned: right value k (0..15) is column wl - dd0 - 8 + k
+    const int gx = w0 + wl;
+    const bool full_cols = gx + VW <= W;
+    const bool plain = gx >= dd0 + ND - 1 && dd0 + ND <= D && full_cols && !scale_div;
+    __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
+
+    auto stage = [&](int hh) {
+        __half* nL = buf + ((hh - h0) % 3) * buf_elems;
+        stage_rows_async(nL, lbase + i64(hh) * W, plane, Cg, w0, tw, W);
+        stage_rows_async(nL + CC * tw, rbase + i64(hh) * W, plane, Cg, w0 - DT, RW, W);
+    };
+    if (h0 < h1) stage(h0);
+    if (h0 + 1 < h1) stage(h0 + 1);
+    for (int h = h0; h < h1; ++h) {
+        const __half* Ls = buf + ((h - h0) % 3) * buf_elems;
+        const __half* Rs = Ls + CC * tw;
+        if (h + 1 < h1) asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+        else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();  // row h landed for every thread; row h - 1's compute done everywhere
+        if (h + 2 < h1) stage(h + 2);  // into row h - 1's buffer
+        float acc[ND][VW];
+#pragma unroll
+        for (int i = 0; i < ND; ++i)
+#pragma unroll
+            for (int v = 0; v < VW; ++v) acc[i][v] = 0.0f;
+#pragma unroll(CG > 0 ? CG : 1)
+        for (int c = 0; c < Cg; ++c) {
+            const uint4 l8 = *reinterpret_cast<const uint4*>(Ls + c * tw + wl);
+            const __half* rp = Rs + c * RW + rs;
+            const uint4 r0 = *reinterpret_cast<const uint4*>(rp);
+            const uint4 r1 = *reinterpret_cast<const uint4*>(rp + 8);
+            unsigned short lv[VW], rv[16];
+            unpack_h2(l8.x, lv[0], lv[1]);
+            unpack_h2(l8.y, lv[2], lv[3]);
+            unpack_h2(l8.z, lv[4], lv[5]);
+            unpack_h2(l8.w, lv[6], lv[7]);
+            unpack_h2(r0.x, rv[0], rv[1]);
+            unpack_h2(r0.y, rv[2], rv[3]);
+            unpack_h2(r0.z, rv[4], rv[5]);
+            unpack_h2(r0.w, rv[6], rv[7]);
+            unpack_h2(r1.x, rv[8], rv[9]);
+            unpack_h2(r1.y, rv[10], rv[11]);
+            unpack_h2(r1.z, rv[12], rv[13]);
+            unpack_h2(r1.w, rv[14], rv[15]);
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd)
+#pragma unroll
+                for (int v = 0; v < VW; ++v) acc[dd][v] = fma_h(lv[v], rv[ND - dd + v], acc[dd][v]);
+        }
+        __half* op = obase + i64(h) * W;
+        if (plain) {
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd) {
+                uint4 u;
+                u.x = scale2_to_half2(acc[dd][0], acc[dd][1], inv_cg);
+                u.y = scale2_to_half2(acc[dd][2], acc[dd][3], inv_cg);
+                u.z = scale2_to_half2(acc[dd][4], acc[dd][5], inv_cg);
+                u.w = scale2_to_half2(acc[dd][6], acc[dd][7], inv_cg);
+                *reinterpret_cast<uint4*>(op + dd * plane) = u;
+            }
+        } else if (gx < W) {
+            const float cg = static_cast<float>(Cg);
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd) {
+                const int d = dd0 + dd;
+                if (d >= D) break;
+                __half tmp[VW];
+#pragma unroll
+                for (int v = 0; v < VW; ++v) {
+                    float val;
+                    if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
+                    else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    tmp[v] = __float2half_rn(val);
+                }
+                __half* o = op + dd * plane;
+                if (full_cols) {
+                    *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(tmp);
+                } else {
+#pragma unroll
+                    for (int v = 0; v < VW; ++v)
+                        if (gx + v < W) o[v] = tmp[v];
+                }
+            }
+        }
+    }
+}
+
 // Small volumes (fewer than kSmallOutputsPerSM outputs per SM; the
 // reference's native 1 x 48 x 32 x 40 is one): one thread per output, both
 // operands read straight through L2, the channel loop unrolled so 8 channels'
@@ -644,6 +762,42 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
         const size_t smem = static_cast<size_t>(cc) * (2 * tw + DT) * 2;
         const int vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
                            (reinterpret_cast<uintptr_t>(right) % 16 == 0);
+        // 8-column x 8-disparity tiles for groups of 8..16 channels and at
+        // most 48 disparities (measured: configs 2 and 4 7 % and 3 % faster;
+        // config 3 (D = 64, fewer resident warps at 121 registers) 23 % and
+        // config 5 (Cg = 4) 11 % slower than the 4 x 8 tile).
+        const int tx8 = tw / 8;
+        const int ny8 = max(1, min((D + kDispPerThread - 1) / kDispPerThread, 512 / tx8));
+        const int DT8 = ny8 * kDispPerThread;
+        if (vec_ok && DT8 >= D && D <= 48 && Cg >= 8 && Cg <= cc) {
+            using RowsFn = void (*)(const __half*, const __half*, __half*, int, int, int, int, int, int, int, int,
+                                    float);
+            RowsFn kern = Cg == 4    ? corr_volume_rows8_kernel<kChunkC, 4>
+                          : Cg == 8  ? corr_volume_rows8_kernel<kChunkC, 8>
+                          : Cg == 12 ? corr_volume_rows8_kernel<kChunkC, 12>
+                          : Cg == 16 ? corr_volume_rows8_kernel<kChunkC, 16>
+                                     : corr_volume_rows8_kernel<kChunkC, 0>;
+            const size_t rsmem = 3 * static_cast<size_t>(cc) * (2 * tw + DT8) * 2;
+            int resident = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, tx8 * ny8, rsmem) != cudaSuccess ||
+                resident < 1)
+                return launch_status("ww_corr_volume");
+            const long long slots = static_cast<long long>(resident) * dev.sm_count;
+            const long long tiles = static_cast<long long>(nt) * B * G;
+            int best = H;
+            long long best_cost = -1;
+            for (int r = 1; r <= H; ++r) {
+                const long long ctas = tiles * ((H + r - 1) / r);
+                const long long cost = ((ctas + slots - 1) / slots) * (r + 1);
+                if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = r; }
+            }
+            dim3 block(tx8, ny8);
+            dim3 grid(nt, (H + best - 1) / best, B * G);
+            kern<<<grid, block, rsmem, stream>>>(static_cast<const __half*>(left), static_cast<const __half*>(right),
+                                                 static_cast<__half*>(out), C, H, W, D, G, best, tw, scale_div,
+                                                 inv_cg);
+            return launch_status("ww_corr_volume");
+        }
         if (vec_ok && n_dband == 1 && Cg <= cc) {
             // Row-streaming form (two staged rows in shared memory): rows
             // per CTA chosen to minimise (waves of resident CTAs) x (rows

@@ -94,6 +94,7 @@ constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
 constexpr int kMaxVBuf = 3;        // volume row buffers
+constexpr int kGroupMinMB = 4;     // M-blocks from which a row is issued and drained as two groups
 constexpr int kMaxFItems = 10 * 24;  // CUDA-core correlation items per job (10 columns x ceil(D/8) + 2 tiles)
 // M-blocks the epilogue drains (tensor memory -> registers, slot released)
 // before it stores any of them.  The MMA warp needs every M-block's slot
@@ -126,6 +127,7 @@ struct StemParams {
     int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
     int n_rbox;               // right boxes of 64 columns per job
     int scale_div;            // CUDA-core correlation: 1 = sum / Cg (rounded division), 0 = sum * (1 / Cg)
+    int n_grp, grp_size;      // M-block groups (1 or 2) with their own completion / release barriers
     int n_fitems;             // CUDA-core correlation: items per job (see corr_item_fma)
     int fma_span;             // CUDA-core correlation: most jobs one producer task touches
     uint32_t tmem_cols;
@@ -517,10 +519,10 @@ __device__ __forceinline__ void issue_row(const StemParams& p, uint32_t tmem_bas
 
 template <int COUTP>
 __device__ __forceinline__ void issue_row_n(const StemParams& p, uint32_t tmem_base, uint64_t a0, uint64_t b0,
-                                            int sn)
+                                            int sn, int nmb)
 {
     // M-block counts the tensor memory holds: NMB * 3 * COUTP <= 512.
-    switch (p.n_mb) {
+    switch (nmb) {
 #define WW_ISSUE_CASE(NMB) \
     case NMB:              \
         if constexpr (NMB * 3 * COUTP <= 512) issue_row<COUTP, NMB>(p, tmem_base, a0, b0, sn); \
@@ -678,9 +680,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     uint64_t* final_bar = bars + 2 * kMaxVBuf;
     uint64_t* stage_full = final_bar + 1;             // [n_slots]
     uint64_t* stage_empty = stage_full + p.n_slots;   // [n_slots]
-    uint64_t* acc_full = stage_empty + p.n_slots;     // one per CTA
-    uint64_t* acc_empty = acc_full + 1;               // one per CTA
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    uint64_t* acc_full = stage_empty + p.n_slots;     // [2]: one per M-block group
+    uint64_t* acc_empty = acc_full + 2;               // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     // ---- set-up: barriers, TMEM, B image, zeroed volume buffers ----
     if (threadIdx.x == 0) {
@@ -693,8 +695,10 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             mbar_init(smem_addr(&stage_empty[i]), kProdWarps);
         }
         mbar_init(smem_addr(final_bar), 1);
-        mbar_init(smem_addr(acc_full), 1);
-        mbar_init(smem_addr(acc_empty), kEpiWarps);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(smem_addr(&acc_full[g]), 1);
+            mbar_init(smem_addr(&acc_empty[g]), kEpiWarps);
+        }
         mbar_fence_init();
     }
     if (warp == kMmaWarp) tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
@@ -855,13 +859,19 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         for (int it = 0; it < n_iter && ok; ++it) {
             const int r = u_first + it - 1;  // output row completed by this volume row
             const int slot = ((r % 3) + 3) % 3;
-            // One commit per row covers every M-block: they complete together
-            // (their last K-step is issued back to back), and a commit per
-            // M-block made the epilogue see them ~0.3-0.5 us apart (measured).
-            if (!warp_wait(smem_addr(acc_full), it & 1, p.err, 1)) break;
+            // One commit per row and M-block group covers the group's
+            // M-blocks: they complete together (their last K-step is issued
+            // back to back), and a commit per M-block made the epilogue see
+            // them ~0.3-0.5 us apart (measured).
+            for (int grp = 0; grp < p.n_grp && ok; ++grp) {
+            const int m_beg = grp * p.grp_size, m_end = min(p.n_mb, m_beg + p.grp_size);
+            if (!warp_wait(smem_addr(&acc_full[grp]), it & 1, p.err, 1)) {
+                ok = false;
+                break;
+            }
             fence_after_sync();
-            for (int m0 = 0; m0 < p.n_mb && ok; m0 += kDrain) {
-                const int mcnt = min(kDrain, p.n_mb - m0);
+            for (int m0 = m_beg; m0 < m_end && ok; m0 += kDrain) {
+                const int mcnt = min(kDrain, m_end - m0);
                 uint32_t ph[kDrain][COUTP / 2];  // fp16 results, packed as (o, o + 1) pairs
                 // With Cout = 16, M-blocks in pairs: both tensor-memory loads
                 // in flight behind one wait (each wait costs a load latency);
@@ -889,10 +899,10 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     for (int h = 0; h < kPair; ++h) reg_fence(acc[h]);  // no use of acc above the wait
                     // The row's slots are free once read: the MMA warp restarts
                     // them with accumulate = 0 (no zeroing here).
-                    if (m0 + j + (two ? 1 : 0) == p.n_mb - 1) {
+                    if (m0 + j + (two ? 1 : 0) == m_end - 1) {
                         fence_before_sync();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(smem_addr(acc_empty));
+                        if (lane == 0) mbar_arrive(smem_addr(&acc_empty[grp]));
                     }
 #pragma unroll
                     for (int h = 0; h < kPair; ++h) {
@@ -946,13 +956,17 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     }
                 }
             }
+            }  // M-block groups
         }
     } else if (warp == kMmaWarp) {
         // ======================= MMA issue =======================
-        // Row by row: once volume row it is produced (vol_full) and the
-        // epilogue has drained every M-block's slot of row it-1 (acc_empty),
-        // issue the row's nsteps K-steps with the n_mb M-blocks interleaved
-        // inside each step.  MMAs into the same accumulator back to back are
+        // Row by row: once volume row it is produced (vol_full), per M-block
+        // group: once the epilogue has drained the group's slots of row it-1
+        // (acc_empty[g]), issue the group's nsteps K-steps with its M-blocks
+        // interleaved inside each step and commit the group (acc_full[g]).
+        // With two groups the epilogue drains group 0 of a row while group
+        // 1's MMAs run, and group 0 of the next row starts without waiting
+        // for group 1's drain.  MMAs into the same accumulator back to back are
         // latency-bound (~150 cycles each); independent ones run at the
         // shared-memory bound (~56 cycles for M=128, N=96), which this order
         // reaches from n_mb = 3 on.  Lane 0 alone runs the loop: a warp-wide
@@ -964,18 +978,28 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             for (int it = 0; it < n_iter; ++it) {
                 const int vb = it % NV;
                 if (!wait_or_fail(smem_addr(&vol_full[vb]), (it / NV) & 1, p.err, 2)) break;
-                if (it > 0 && !wait_or_fail(smem_addr(acc_empty), (it - 1) & 1, p.err, 3)) break;
-                fence_after_sync();
                 const int u = u_first + it;
-                if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
-                    const int rot = (((1 - u) % 3) + 3) % 3;
-                    const uint64_t a0 = vol_base + static_cast<uint64_t>((vb * p.vol_buf_bytes) >> 4);
-                    const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
-                    // K-step 0 starts output row u+1 in its slot (u+1) mod 3 (it
-                    // still holds the row the epilogue drained).
-                    issue_row_n<COUTP>(p, tmem_base, a0, b0, (u + 1) % 3);
+                bool row_ok = true;
+                for (int grp = 0; grp < p.n_grp; ++grp) {
+                    if (it > 0 && !wait_or_fail(smem_addr(&acc_empty[grp]), (it - 1) & 1, p.err, 3)) {
+                        row_ok = false;
+                        break;
+                    }
+                    fence_after_sync();
+                    if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
+                        const int m0 = grp * p.grp_size;
+                        const int rot = (((1 - u) % 3) + 3) % 3;
+                        const uint64_t a0 = vol_base + static_cast<uint64_t>((vb * p.vol_buf_bytes) >> 4) +
+                                            static_cast<uint64_t>(m0) * ((16 * kWtp * 16) >> 4);
+                        const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
+                        // K-step 0 starts output row u+1 in its slot (u+1) mod 3 (it
+                        // still holds the row the epilogue drained).
+                        issue_row_n<COUTP>(p, tmem_base + static_cast<uint32_t>(m0 * 3 * COUTP), a0, b0, (u + 1) % 3,
+                                           min(p.grp_size, p.n_mb - m0));
+                    }
+                    mma_commit(smem_addr(&acc_full[grp]));
                 }
-                mma_commit(smem_addr(acc_full));
+                if (!row_ok) break;
                 mma_commit(smem_addr(&vol_empty[vb]));
             }
         }
@@ -1254,7 +1278,7 @@ int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexc
     o = (o + 127) & ~127LL;
     o += 2 * vol_buf;
     o = (o + 127) & ~127LL;
-    o += 128 + (2 * kMaxVBuf + 1 + 2 * kMaxSlots + 2) * 8 + 16;
+    o += 128 + (2 * kMaxVBuf + 1 + 2 * kMaxSlots + 4) * 8 + 16;
     o = (o + 15) & ~15LL;
     o += coutp * 4;
     o = (o + 1023) & ~1023LL;
@@ -1315,6 +1339,10 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.B = B; p.C = C; p.G = G; p.H = H; p.W = W; p.D = D; p.Cout = Cout; p.act = act;
     p.in_row0 = in_row0; p.in_rows = in_rows; p.out_row0 = out_row0; p.out_rows = out_rows;
     p.Cg = Cg; p.KG = KG; p.Dp = Dp; p.n_mb = n_mb; p.nsteps = nsteps;
+    // Two M-block groups from kGroupMinMB M-blocks on (each group keeps at
+    // least two M-blocks interleaved, so its MMAs stay independent).
+    p.n_grp = n_mb >= kGroupMinMB ? 2 : 1;
+    p.grp_size = (n_mb + p.n_grp - 1) / p.n_grp;
     p.n_wtiles = (W + kWt - 1) / kWt;
     // The fused correlation scales by * (1 / Cg): exactly / Cg when Cg is a
     // power of two, within one fp32 ulp of it otherwise (the tensor-core sums
@@ -1339,7 +1367,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
     p.stage_slot_bytes = fused ? ((p.off_l + 8u * Cg * kLRowBytes + 1023) / 1024) * 1024 : 0;
     p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + kLStageW) * 8 * Cg * 2);
-    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 2) * 8 + 16); };
+    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 4) * 8 + 16); };
     auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
         uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
         o = (o + 127) & ~127u;

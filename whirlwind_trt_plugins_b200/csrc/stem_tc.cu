@@ -95,6 +95,7 @@ constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
 constexpr int kMaxVBuf = 3;        // volume row buffers
 constexpr int kGroupMinMB = 4;     // M-blocks from which a row is issued and drained as two groups
+constexpr bool kDualTiles = true;  // two 8-column tiles per CTA where tensor memory holds them
 constexpr int kMaxFItems = 10 * 24;  // CUDA-core correlation items per job (10 columns x ceil(D/8) + 2 tiles)
 // M-blocks the epilogue drains (tensor memory -> registers, slot released)
 // before it stores any of them.  The MMA warp needs every M-block's slot
@@ -128,6 +129,10 @@ struct StemParams {
     int n_rbox;               // right boxes of 64 columns per job
     int scale_div;            // CUDA-core correlation: 1 = sum / Cg (rounded division), 0 = sum * (1 / Cg)
     int n_grp, grp_size;      // M-block groups (1 or 2) with their own completion / release barriers
+    int ntile;                // 8-column tiles per CTA (1, or 2: one M-block group per tile)
+    int l_stage_w;            // staged left columns [w0 - 8, w0 + l_stage_w - 8)
+    int l_row_bytes;          // 2 * l_stage_w
+    uint32_t tile_vol_bytes;  // one tile's part of a volume buffer
     int n_fitems;             // CUDA-core correlation: items per job (see corr_item_fma)
     int fma_span;             // CUDA-core correlation: most jobs one producer task touches
     uint32_t tmem_cols;
@@ -340,9 +345,11 @@ __device__ __forceinline__ uint32_t rchunk(uint32_t rb, int r, int jt, uint32_t 
 // KM = 8: Cg <= 8 (m16n8k8); KM = 16: 8 < Cg <= 16 (m16n8k16).  FULL: Cg ==
 // KM (no absent channels); otherwise channels >= Cg read zeros (A:
 // predicated loads; B: a zeroed 128-byte row).
+// tl: the CTA's column tile (its left columns start 8 tl further right, and
+// its right tile jt is staged tile jt + tl).
 template <int KM, bool FULL>
 __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
-                                              uint32_t vsa, int jt0, int jt1, int lane)
+                                              uint32_t vsa, int jt0, int jt1, int lane, int tl)
 {
     constexpr int NA = KM == 8 ? 2 : 4;  // A registers per group
     constexpr int NB = KM == 8 ? 1 : 2;  // B registers per group and tile
@@ -364,7 +371,7 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
             const int e = KM == 8 ? 4 * j + mi : 2 * j + (mi >> 1);
             const int c = KM == 8 ? rr : 8 * (mi & 1) + rr;
             const uint32_t addr = (FULL || c < Cg)
-                                      ? lslot + static_cast<uint32_t>((e * Cg + c) * kLRowBytes + 16)
+                                      ? lslot + static_cast<uint32_t>((e * Cg + c) * p.l_row_bytes + 16 + 16 * tl)
                                       : zero_row;
             uint32_t r4[4];
             ldmatrix_x4_trans(addr, r4);
@@ -374,15 +381,15 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
                 else a[2 * j + (k >> 1)][2 * (k & 1)] = r4[k];
             }
         }
-        const int col = m == 0 ? 7 : 16;  // staged left column of row 8 + m
+        const int col = (m == 0 ? 7 : 16) + 8 * tl;  // staged left column of row 8 + m
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
 #pragma unroll
             for (int r = 1; r < NA; r += 2) {
                 const int c0 = 2 * q + 8 * (r >> 1);
-                const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * col);
+                const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * p.l_row_bytes + 2 * col);
                 const unsigned short lo = (m < 2 && (FULL || c0 < Cg)) ? ld_shared_u16(la) : 0;
-                const unsigned short hi = (m < 2 && (FULL || c0 + 1 < Cg)) ? ld_shared_u16(la + kLRowBytes) : 0;
+                const unsigned short hi = (m < 2 && (FULL || c0 + 1 < Cg)) ? ld_shared_u16(la + p.l_row_bytes) : 0;
                 a[e][r] = pack_b16x2(lo, hi);
             }
         }
@@ -407,8 +414,8 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
 #pragma unroll
         for (int k = 0; k < NI; ++k) {
             uint32_t r4[4];
-            const uint32_t addr = (FULL || rrow[k] >= 0) ? rchunk(rb[k], rrow[k], jt, p.rbox_bytes)
-                                                         : rb[k] + (static_cast<uint32_t>(jt & 7) << 4);
+            const uint32_t addr = (FULL || rrow[k] >= 0) ? rchunk(rb[k], rrow[k], jt + tl, p.rbox_bytes)
+                                                         : rb[k] + (static_cast<uint32_t>((jt + tl) & 7) << 4);
             ldmatrix_x4_trans(addr, r4);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -431,7 +438,7 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
 // Cg > 16: the channels run through the tensor core in chunks of 16 (the
 // last one zero-padded), with the fragments of each chunk loaded per tile.
 __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t slot, uint32_t zero_row,
-                                                   uint32_t vsa, int jt0, int jt1, int lane)
+                                                   uint32_t vsa, int jt0, int jt1, int lane, int tl)
 {
     const int m = lane >> 2, q = lane & 3;
     const int mi = lane >> 3, rr = lane & 7;
@@ -452,8 +459,8 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                 const int c = kc + 8 * (mi & 1) + rr;
                 const int r = e * Cg + c;
                 uint32_t r4[4];
-                ldmatrix_x4_trans(c < Cg ? rchunk(slot + static_cast<uint32_t>(r) * 128u, r, jt, p.rbox_bytes)
-                                         : zero_row + (static_cast<uint32_t>(jt & 7) << 4),
+                ldmatrix_x4_trans(c < Cg ? rchunk(slot + static_cast<uint32_t>(r) * 128u, r, jt + tl, p.rbox_bytes)
+                                         : zero_row + (static_cast<uint32_t>((jt + tl) & 7) << 4),
                                   r4);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) b[2 * k + (i >> 1)][i & 1] = r4[i];
@@ -466,11 +473,11 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                     // row m (r even) or 8 + m (r odd) of the tile: see tile_row_wp
                     const int c0 = kc + 2 * q + 8 * (r >> 1);
                     const bool top = (r & 1) == 0;
-                    const int col = top ? m + 8 : (m == 0 ? 7 : 16);
+                    const int col = (top ? m + 8 : (m == 0 ? 7 : 16)) + 8 * tl;
                     const bool row_ok = top || m < 2;
-                    const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * kLRowBytes + 2 * col);
+                    const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * p.l_row_bytes + 2 * col);
                     const unsigned short lo = (row_ok && c0 < Cg) ? ld_shared_u16(la) : 0;
-                    const unsigned short hi = (row_ok && c0 + 1 < Cg) ? ld_shared_u16(la + kLRowBytes) : 0;
+                    const unsigned short hi = (row_ok && c0 + 1 < Cg) ? ld_shared_u16(la + p.l_row_bytes) : 0;
                     a[r] = pack_b16x2(lo, hi);
                 }
                 mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
@@ -561,7 +568,7 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
     // 16-byte chunk (jt % 8) ^ (r % 8) of the row (128-byte TMA swizzle).
     const uint8_t* rbox = stage + (jt >> 3) * p.rbox_bytes + 4 * q * Cg * 128;
     const uint32_t jsw = static_cast<uint32_t>(jt & 7);
-    const uint8_t* lcol = stage + p.off_l + 2 * (wp + 7) + 4 * q * Cg * kLRowBytes;  // staged column w' + 7
+    const uint8_t* lcol = stage + p.off_l + 2 * (wp + 7) + 4 * q * Cg * p.l_row_bytes;  // staged column w' + 7
     const int rq = 4 * q * Cg;  // first row of the half
     float acc[4][8];
 #pragma unroll
@@ -575,7 +582,7 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
             const int rl = e * Cg + c;  // row within the half
             const uint32_t sw = ((jsw ^ static_cast<uint32_t>((rq + rl) & 7)) << 4);
             const uint4 rv = *reinterpret_cast<const uint4*>(rbox + rl * 128 + sw);
-            const unsigned short lv = *reinterpret_cast<const unsigned short*>(lcol + rl * kLRowBytes);
+            const unsigned short lv = *reinterpret_cast<const unsigned short*>(lcol + rl * p.l_row_bytes);
             unsigned short h[8];
             unpack_b16x2(rv.x, h[0], h[1]);
             unpack_b16x2(rv.y, h[2], h[3]);
@@ -613,13 +620,13 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
 // (corr_item_fma): 6: Cg == 8, 7: Cg == 4, 8: Cg == 12, 9: Cg == 16, 10: any.
 template <int CORR>
 __device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, uint32_t zero_row, uint32_t vsa,
-                                          int jt0, int jt1, int lane)
+                                          int jt0, int jt1, int lane, int tl)
 {
-    if constexpr (CORR == 1) corr_task_mma<8, true>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 2) corr_task_mma<8, false>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 3) corr_task_mma<16, true>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else if constexpr (CORR == 4) corr_task_mma<16, false>(p, slot, zero_row, vsa, jt0, jt1, lane);
-    else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane);
+    if constexpr (CORR == 1) corr_task_mma<8, true>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 2) corr_task_mma<8, false>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 3) corr_task_mma<16, true>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 4) corr_task_mma<16, false>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
 }
 
 template <int CORR>
@@ -661,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     t /= p.n_wtiles;
     const int strip = t % p.n_strips;
     const int b = t / p.n_strips;
-    const int w0 = wt * kWt;
+    const int w0 = wt * kWt * p.ntile;
     const int r0 = p.out_row0 + strip * p.strip;                    // first output row
     const int r1 = min(r0 + p.strip, p.out_row0 + p.out_rows);     // one past last
     const int u_first = r0 - 1;
@@ -834,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         // Zero this quadrant's lanes of every accumulator column.
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
         const uint32_t zeros[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int c = 0; c < p.n_mb * N; c += 8) tmem_st8(lane_base + c, zeros);
+        for (int c = 0; c < p.ntile * p.n_mb * N; c += 8) tmem_st8(lane_base + c, zeros);
         tmem_wait_st();
     }
     fence_before_sync();
@@ -850,7 +857,6 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
         constexpr int kDrain = drain_blocks<COUTP>();
         const int rr = warp * 32 + lane;  // M row
-        const int w = w0 + (rr & 7);
         const int dsub = rr >> 3;         // 0..15
         const float* sbias = reinterpret_cast<const float*>(smem + p.off_bias);
         const int64_t plane_out = i64(p.out_rows) * p.W;
@@ -864,7 +870,13 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             // back to back), and a commit per M-block made the epilogue see
             // them ~0.3-0.5 us apart (measured).
             for (int grp = 0; grp < p.n_grp && ok; ++grp) {
-            const int m_beg = grp * p.grp_size, m_end = min(p.n_mb, m_beg + p.grp_size);
+            // Two tiles: group = tile, every M-block; one tile: M-block ranges.
+            const int tile = p.ntile == 2 ? grp : 0;
+            const int m_beg = p.ntile == 2 ? 0 : grp * p.grp_size;
+            const int m_end = p.ntile == 2 ? p.n_mb : min(p.n_mb, m_beg + p.grp_size);
+            const int w0t = w0 + kWt * tile;  // the tile's first column
+            const int w = w0t + (rr & 7);
+            const uint32_t tile_cols = static_cast<uint32_t>(tile * p.n_mb * N);
             if (!warp_wait(smem_addr(&acc_full[grp]), it & 1, p.err, 1)) {
                 ok = false;
                 break;
@@ -885,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
 #pragma unroll
                     for (int h = 0; h < kPair; ++h) {
                         if (h == 1 && !two) break;
-                        const uint32_t col = lane_base + (m0 + j + h) * N + slot * COUTP;
+                        const uint32_t col = lane_base + tile_cols + (m0 + j + h) * N + slot * COUTP;
 #pragma unroll
                         for (int c = 0; c < COUTP; c += 16) {
                             uint32_t v16[16];
@@ -942,9 +954,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                             const uint4 hi =
                                 make_uint4(__byte_perm(e[0], e[1], 0x7632), __byte_perm(e[2], e[3], 0x7632),
                                            __byte_perm(e[4], e[5], 0x7632), __byte_perm(e[6], e[7], 0x7632));
-                            if (d < p.D && o0 < p.Cout) *reinterpret_cast<uint4*>(orow + o0 * ostride + w0) = lo;
-                            if (d < p.D && o0 + 1 < p.Cout)
-                                *reinterpret_cast<uint4*>(orow + (o0 + 1) * ostride + w0) = hi;
+                            if (d < p.D && o0 < p.Cout && w0t < p.W) *reinterpret_cast<uint4*>(orow + o0 * ostride + w0t) = lo;
+                            if (d < p.D && o0 + 1 < p.Cout && w0t < p.W)
+                                *reinterpret_cast<uint4*>(orow + (o0 + 1) * ostride + w0t) = hi;
                         }
                     } else if (d < p.D && w < p.W) {
 #pragma unroll
@@ -987,15 +999,18 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     }
                     fence_after_sync();
                     if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
-                        const int m0 = grp * p.grp_size;
+                        const int tile = p.ntile == 2 ? grp : 0;
+                        const int m0 = p.ntile == 2 ? 0 : grp * p.grp_size;
+                        const int cnt = p.ntile == 2 ? p.n_mb : min(p.grp_size, p.n_mb - m0);
                         const int rot = (((1 - u) % 3) + 3) % 3;
                         const uint64_t a0 = vol_base + static_cast<uint64_t>((vb * p.vol_buf_bytes) >> 4) +
+                                            static_cast<uint64_t>((tile * p.tile_vol_bytes) >> 4) +
                                             static_cast<uint64_t>(m0) * ((16 * kWtp * 16) >> 4);
                         const uint64_t b0 = b_base + static_cast<uint64_t>((rot * COUTP * 16) >> 4);
                         // K-step 0 starts output row u+1 in its slot (u+1) mod 3 (it
                         // still holds the row the epilogue drained).
-                        issue_row_n<COUTP>(p, tmem_base + static_cast<uint32_t>(m0 * 3 * COUTP), a0, b0, (u + 1) % 3,
-                                           min(p.grp_size, p.n_mb - m0));
+                        issue_row_n<COUTP>(p, tmem_base + static_cast<uint32_t>((tile * p.n_mb + m0) * 3 * COUTP), a0, b0,
+                                           (u + 1) % 3, cnt);
                     }
                     mma_commit(smem_addr(&acc_full[grp]));
                 }
@@ -1036,11 +1051,12 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     const int g = kg * 8 + ge;
                     const bool gv = g < p.G;
                     const int64_t roff = ((i64(b) * p.C + (gv ? g * Cg + cc : 0)) * p.in_rows + urow) * p.W;
-                    for (int v = 0; v < 3 + nvr; ++v) {
-                        const bool isL = v < 3;
-                        const int x = isL ? (w0 - 8 + 8 * v) : (rbase + 8 * (v - 3));
-                        const uint32_t dst = isL ? sbase + p.off_l + lc * kLRowBytes + 16 * v
-                                                 : rchunk(sbase + lc * 128u, lc, v - 3, p.rbox_bytes);
+                    const int nlv = p.l_stage_w / 8;
+                    for (int v = 0; v < nlv + nvr; ++v) {
+                        const bool isL = v < nlv;
+                        const int x = isL ? (w0 - 8 + 8 * v) : (rbase + 8 * (v - nlv));
+                        const uint32_t dst = isL ? sbase + p.off_l + lc * p.l_row_bytes + 16 * v
+                                                 : rchunk(sbase + lc * 128u, lc, v - nlv, p.rbox_bytes);
                         const __half* srow = (isL ? p.left : p.right) + roff;
                         if (p.vec_ok) {
                             const bool in = gv && x >= 0 && x < p.W;  // whole vector (W % 8 == 0)
@@ -1149,11 +1165,15 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         }
                         const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
                         const uint32_t vsa = smem_addr(vbuf + kg * p.lbo_vol);
-                        // this warp's tasks of the job: tau = job * tpj + h, tau % kProdWarps == pw
-                        for (int h = ((pw - job * p.tpj) % kProdWarps + kProdWarps) % kProdWarps; h < p.tpj;
-                             h += kProdWarps) {
-                            const int jt0 = (h * p.n_tiles) / p.tpj, jt1 = ((h + 1) * p.n_tiles) / p.tpj;
-                            corr_task<CORR>(p, sbase, zero_row, vsa, jt0, jt1, lane);
+                        // this warp's tasks of the job: tau = job * T + h with
+                        // T = tpj * ntile tasks per job, tau % kProdWarps == pw;
+                        // task h is range h % tpj of tile h / tpj.
+                        const int T = p.tpj * p.ntile;
+                        for (int h = ((pw - job * T) % kProdWarps + kProdWarps) % kProdWarps; h < T; h += kProdWarps) {
+                            const int tl = h / p.tpj, hh = h - tl * p.tpj;
+                            const int jt0 = (hh * p.n_tiles) / p.tpj, jt1 = ((hh + 1) * p.n_tiles) / p.tpj;
+                            corr_task<CORR>(p, sbase, zero_row, vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes, jt0,
+                                            jt1, lane, tl);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
@@ -1339,11 +1359,6 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.B = B; p.C = C; p.G = G; p.H = H; p.W = W; p.D = D; p.Cout = Cout; p.act = act;
     p.in_row0 = in_row0; p.in_rows = in_rows; p.out_row0 = out_row0; p.out_rows = out_rows;
     p.Cg = Cg; p.KG = KG; p.Dp = Dp; p.n_mb = n_mb; p.nsteps = nsteps;
-    // Two M-block groups from kGroupMinMB M-blocks on (each group keeps at
-    // least two M-blocks interleaved, so its MMAs stay independent).
-    p.n_grp = n_mb >= kGroupMinMB ? 2 : 1;
-    p.grp_size = (n_mb + p.n_grp - 1) / p.n_grp;
-    p.n_wtiles = (W + kWt - 1) / kWt;
     // The fused correlation scales by * (1 / Cg): exactly / Cg when Cg is a
     // power of two, within one fp32 ulp of it otherwise (the tensor-core sums
     // already differ from CorrVolume's fp32 chain at that level), and without
@@ -1351,50 +1366,78 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.inv_cg = 1.0f / static_cast<float>(Cg);
     p.vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
                (reinterpret_cast<uintptr_t>(right) % 16 == 0);
-    p.rstage_w = 16 + 8 * ((D + 7) / 8);  // right columns [w0 - 8*ceil(D/8), w0 + 16)
-    p.tmem_cols = pow2_cols(static_cast<uint32_t>(n_mb * 3 * coutp));
+    const bool cuda_core_corr = fused && g_corr_engine.load(std::memory_order_relaxed) == WW_CORR_ENGINE_CUDA_CORES;
 
-    // shared-memory layout: B image | 2 or 3 volume buffers | zero row,
-    // barriers | staging ring (1024-byte aligned slots for the 128-byte TMA
-    // swizzle).  Three volume buffers when three staging slots still fit.
-    p.lbo_vol = static_cast<uint32_t>((Dp + 2) * kWtp * 16);
-    // + a zeroed 128-byte guard: the zero-weight partner of a lone octet
-    // (step_info, t1 < 0) reads one 16-byte position past the last plane.
-    p.vol_buf_bytes = p.lbo_vol * KG + 128;
-    p.n_tiles = (D + 7) / 8 + 2;
-    p.n_rbox = (p.rstage_w + 63) / 64;
-    p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
-    p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
-    p.stage_slot_bytes = fused ? ((p.off_l + 8u * Cg * kLRowBytes + 1023) / 1024) * 1024 : 0;
-    p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + kLStageW) * 8 * Cg * 2);
-    auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 4) * 8 + 16); };
-    auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
-        uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
-        o = (o + 127) & ~127u;
-        p.off_vol = o;
-        o += static_cast<uint32_t>(nv) * p.vol_buf_bytes;
-        o = (o + 127) & ~127u;
-        p.off_zero = o;
-        o += 128;
-        p.off_bar = o;
-        o += bar_bytes(kMaxSlots);
-        o = (o + 15) & ~15u;
-        p.off_bias = o;
-        o += static_cast<uint32_t>(coutp) * 4;
-        return (o + 1023) & ~1023u;
+    // Geometry for nt 8-column tiles per CTA; returns the dynamic shared
+    // memory, or 0 when it does not fit (or, for two tiles, leaves fewer
+    // than three staging slots).  Shared-memory layout: B image | 2 or 3
+    // volume buffers (each nt tiles) | zero row, barriers, bias | staging ring
+    // (1024-byte aligned slots for the 128-byte TMA swizzle).  Three volume
+    // buffers when three staging slots still fit.
+    auto geometry = [&](int nt) -> size_t {
+        p.ntile = nt;
+        p.l_stage_w = kLStageW + kWt * (nt - 1);    // left columns [w0 - 8, w0 + 8 nt + 8)
+        p.l_row_bytes = 2 * p.l_stage_w;
+        p.n_wtiles = (W + kWt * nt - 1) / (kWt * nt);
+        p.rstage_w = 16 + 8 * ((D + 7) / 8) + kWt * (nt - 1);  // right columns [w0 - 8 ceil(D/8), w0 + 8 nt + 8)
+        p.tmem_cols = pow2_cols(static_cast<uint32_t>(nt * n_mb * 3 * coutp));
+        p.lbo_vol = static_cast<uint32_t>((Dp + 2) * kWtp * 16);
+        // + a zeroed 128-byte guard per tile: the zero-weight partner of a lone
+        // octet (step_info, t1 < 0) reads one 16-byte position past the last plane.
+        p.tile_vol_bytes = p.lbo_vol * KG + 128;
+        p.vol_buf_bytes = static_cast<uint32_t>(nt) * p.tile_vol_bytes;
+        p.n_tiles = (D + 7) / 8 + 2;
+        p.n_rbox = (p.rstage_w + 63) / 64;
+        p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
+        p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
+        p.stage_slot_bytes =
+            fused ? ((p.off_l + 8u * Cg * static_cast<uint32_t>(p.l_row_bytes) + 1023) / 1024) * 1024 : 0;
+        p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + p.l_stage_w) * 8 * Cg * 2);
+        auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 4) * 8 + 16); };
+        auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
+            uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
+            o = (o + 127) & ~127u;
+            p.off_vol = o;
+            o += static_cast<uint32_t>(nv) * p.vol_buf_bytes;
+            o = (o + 127) & ~127u;
+            p.off_zero = o;
+            o += 128;
+            p.off_bar = o;
+            o += bar_bytes(kMaxSlots);
+            o = (o + 15) & ~15u;
+            p.off_bias = o;
+            o += static_cast<uint32_t>(coutp) * 4;
+            return (o + 1023) & ~1023u;
+        };
+        p.n_vbuf = (layout(3) + 3 * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin)) ? 3 : 2;
+        uint32_t off = layout(p.n_vbuf);
+        p.off_b = 0;
+        p.off_stage = off;
+        // as many staging slots (2..kMaxSlots) as shared memory holds
+        p.n_slots = 2;
+        while (fused && p.n_slots < kMaxSlots &&
+               off + (p.n_slots + 1) * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin))
+            ++p.n_slots;
+        off += fused ? p.n_slots * p.stage_slot_bytes : 0;
+        if (off > static_cast<uint32_t>(dev.smem_optin)) return 0;
+        if (nt == 2 && p.n_slots < 3) return 0;
+        return off;
     };
-    p.n_vbuf = (layout(3) + 3 * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin)) ? 3 : 2;
-    uint32_t off = layout(p.n_vbuf);
-    p.off_b = 0;
-    p.off_stage = off;
-    // as many staging slots (2..kMaxSlots) as shared memory holds
-    p.n_slots = 2;
-    while (fused && p.n_slots < kMaxSlots &&
-           off + (p.n_slots + 1) * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin))
-        ++p.n_slots;
-    off += fused ? p.n_slots * p.stage_slot_bytes : 0;
-    const size_t smem = off;
-    if (smem > static_cast<size_t>(dev.smem_optin)) return WW_ERR_UNSUPPORTED;
+    // Two column tiles per CTA when their accumulators fit tensor memory
+    // (Cout <= 16, D <= 80) and the tensor-core correlation runs: the right
+    // window staged per job then serves 16 output columns instead of 8, and
+    // one tile's drain overlaps the other's MMAs.
+    size_t smem = 0;
+    if (fused && kDualTiles && !cuda_core_corr && coutp == 16 && Cg <= 16 && W > kWt &&
+        2 * n_mb * 3 * coutp <= 512)
+        smem = geometry(2);
+    if (smem == 0) smem = geometry(1);
+    if (smem == 0) return WW_ERR_UNSUPPORTED;
+    // M-block groups: one per tile with two tiles; otherwise two from
+    // kGroupMinMB M-blocks on (each group keeps at least two M-blocks
+    // interleaved, so its MMAs stay independent).
+    p.n_grp = p.ntile == 2 ? 2 : (n_mb >= kGroupMinMB ? 2 : 1);
+    p.grp_size = p.ntile == 2 ? n_mb : (n_mb + p.n_grp - 1) / p.n_grp;
     // Tasks per job: two right tiles per task.  A task loads its octet's left
     // (A) fragments once for all its tiles, so two tiles per task halve those
     // loads, while half the producer warps per job still keep a job's latency
@@ -1403,7 +1446,6 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.tpj = (p.n_tiles + 1) / 2;
     // CUDA-core correlation items: (right tile, volume column) pairs with
     // any disparity in [0, D), and the most jobs a task of 32 items touches.
-    const bool cuda_core_corr = fused && g_corr_engine.load(std::memory_order_relaxed) == WW_CORR_ENGINE_CUDA_CORES;
     p.n_fitems = 0;
     p.fma_span = 0;
     p.scale_div = 0;
@@ -1435,7 +1477,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     }
     p.use_tma = 0;
     if (fused && p.vec_ok && 8 * Cg <= 256) {
-        p.use_tma = encode_feature_map(&p.tmap_l, left, B, C, in_rows, W, kLStageW, 8 * Cg, false) &&
+        p.use_tma = encode_feature_map(&p.tmap_l, left, B, C, in_rows, W, p.l_stage_w, 8 * Cg, false) &&
                     encode_feature_map(&p.tmap_r, right, B, C, in_rows, W, 64, 8 * Cg, true);
     }
 

@@ -347,10 +347,12 @@ __device__ __forceinline__ uint32_t rchunk(uint32_t rb, int r, int jt, uint32_t 
 // predicated loads; B: a zeroed 128-byte row).
 // tl: the CTA's column tile (its left columns start 8 tl further right, and
 // its right tile jt is staged tile jt + tl).
-template <int KM, bool FULL>
+template <int KM, bool FULL, int NT>
 __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                               uint32_t vsa, int jt0, int jt1, int lane, int tl)
 {
+    constexpr int LRB = 2 * (kLStageW + kWt * (NT - 1));  // staged left row bytes
+    if constexpr (NT == 1) tl = 0;
     constexpr int NA = KM == 8 ? 2 : 4;  // A registers per group
     constexpr int NB = KM == 8 ? 1 : 2;  // B registers per group and tile
     constexpr int NI = KM == 8 ? 2 : 4;  // ldmatrix.x4 per tile
@@ -371,7 +373,7 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
             const int e = KM == 8 ? 4 * j + mi : 2 * j + (mi >> 1);
             const int c = KM == 8 ? rr : 8 * (mi & 1) + rr;
             const uint32_t addr = (FULL || c < Cg)
-                                      ? lslot + static_cast<uint32_t>((e * Cg + c) * p.l_row_bytes + 16 + 16 * tl)
+                                      ? lslot + static_cast<uint32_t>((e * Cg + c) * LRB + 16 + 16 * tl)
                                       : zero_row;
             uint32_t r4[4];
             ldmatrix_x4_trans(addr, r4);
@@ -387,9 +389,9 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
 #pragma unroll
             for (int r = 1; r < NA; r += 2) {
                 const int c0 = 2 * q + 8 * (r >> 1);
-                const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * p.l_row_bytes + 2 * col);
+                const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * LRB + 2 * col);
                 const unsigned short lo = (m < 2 && (FULL || c0 < Cg)) ? ld_shared_u16(la) : 0;
-                const unsigned short hi = (m < 2 && (FULL || c0 + 1 < Cg)) ? ld_shared_u16(la + p.l_row_bytes) : 0;
+                const unsigned short hi = (m < 2 && (FULL || c0 + 1 < Cg)) ? ld_shared_u16(la + LRB) : 0;
                 a[e][r] = pack_b16x2(lo, hi);
             }
         }
@@ -438,8 +440,10 @@ __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot
 // Cg > 16: the channels run through the tensor core in chunks of 16 (the
 // last one zero-padded), with the fragments of each chunk loaded per tile.
 __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t slot, uint32_t zero_row,
-                                                   uint32_t vsa, int jt0, int jt1, int lane, int tl)
+                                                   uint32_t vsa, int jt0, int jt1, int lane)
 {
+    constexpr int tl = 0;          // Cg > 16: one column tile per CTA
+    constexpr int LRB = 2 * kLStageW;
     const int m = lane >> 2, q = lane & 3;
     const int mi = lane >> 3, rr = lane & 7;
     const int Cg = p.Cg;
@@ -475,9 +479,9 @@ __device__ __forceinline__ void corr_task_mma_wide(const StemParams& p, uint32_t
                     const bool top = (r & 1) == 0;
                     const int col = (top ? m + 8 : (m == 0 ? 7 : 16)) + 8 * tl;
                     const bool row_ok = top || m < 2;
-                    const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * p.l_row_bytes + 2 * col);
+                    const uint32_t la = lslot + static_cast<uint32_t>((e * Cg + c0) * LRB + 2 * col);
                     const unsigned short lo = (row_ok && c0 < Cg) ? ld_shared_u16(la) : 0;
-                    const unsigned short hi = (row_ok && c0 + 1 < Cg) ? ld_shared_u16(la + p.l_row_bytes) : 0;
+                    const unsigned short hi = (row_ok && c0 + 1 < Cg) ? ld_shared_u16(la + LRB) : 0;
                     a[r] = pack_b16x2(lo, hi);
                 }
                 mma_16x8x16_f16f32(acc[e], a[0], a[1], a[2], a[3], b[e][0], b[e][1]);
@@ -568,7 +572,8 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
     // 16-byte chunk (jt % 8) ^ (r % 8) of the row (128-byte TMA swizzle).
     const uint8_t* rbox = stage + (jt >> 3) * p.rbox_bytes + 4 * q * Cg * 128;
     const uint32_t jsw = static_cast<uint32_t>(jt & 7);
-    const uint8_t* lcol = stage + p.off_l + 2 * (wp + 7) + 4 * q * Cg * p.l_row_bytes;  // staged column w' + 7
+    constexpr int LRB = 2 * kLStageW;  // the CUDA-core engine runs one column tile per CTA
+    const uint8_t* lcol = stage + p.off_l + 2 * (wp + 7) + 4 * q * Cg * LRB;  // staged column w' + 7
     const int rq = 4 * q * Cg;  // first row of the half
     float acc[4][8];
 #pragma unroll
@@ -582,7 +587,7 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
             const int rl = e * Cg + c;  // row within the half
             const uint32_t sw = ((jsw ^ static_cast<uint32_t>((rq + rl) & 7)) << 4);
             const uint4 rv = *reinterpret_cast<const uint4*>(rbox + rl * 128 + sw);
-            const unsigned short lv = *reinterpret_cast<const unsigned short*>(lcol + rl * p.l_row_bytes);
+            const unsigned short lv = *reinterpret_cast<const unsigned short*>(lcol + rl * LRB);
             unsigned short h[8];
             unpack_b16x2(rv.x, h[0], h[1]);
             unpack_b16x2(rv.y, h[2], h[3]);
@@ -618,15 +623,15 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
 // carries only its own producer path).  Warp-level tensor cores: 1: Cg == 8,
 // 2: Cg < 8, 3: Cg == 16, 4: 8 < Cg < 16, 5: Cg > 16.  CUDA cores
 // (corr_item_fma): 6: Cg == 8, 7: Cg == 4, 8: Cg == 12, 9: Cg == 16, 10: any.
-template <int CORR>
+template <int CORR, int NT>
 __device__ __forceinline__ void corr_task(const StemParams& p, uint32_t slot, uint32_t zero_row, uint32_t vsa,
                                           int jt0, int jt1, int lane, int tl)
 {
-    if constexpr (CORR == 1) corr_task_mma<8, true>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
-    else if constexpr (CORR == 2) corr_task_mma<8, false>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
-    else if constexpr (CORR == 3) corr_task_mma<16, true>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
-    else if constexpr (CORR == 4) corr_task_mma<16, false>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
-    else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    if constexpr (CORR == 1) corr_task_mma<8, true, NT>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 2) corr_task_mma<8, false, NT>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 3) corr_task_mma<16, true, NT>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else if constexpr (CORR == 4) corr_task_mma<16, false, NT>(p, slot, zero_row, vsa, jt0, jt1, lane, tl);
+    else corr_task_mma_wide(p, slot, zero_row, vsa, jt0, jt1, lane);
 }
 
 template <int CORR>
@@ -649,7 +654,9 @@ inline int corr_variant(int Cg, bool cuda_cores)
 }
 
 // CORR: correlation variant (fused mode; 0 in volume mode).
-template <int COUTP, bool FUSED, int CORR>
+// NT: 8-column tiles per CTA (2 only for Cout <= 16 with the tensor-core
+// correlation variants 1-4).
+template <int COUTP, bool FUSED, int CORR, int NT>
 __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_constant__ StemParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -668,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     t /= p.n_wtiles;
     const int strip = t % p.n_strips;
     const int b = t / p.n_strips;
-    const int w0 = wt * kWt * p.ntile;
+    const int w0 = wt * kWt * NT;
     const int r0 = p.out_row0 + strip * p.strip;                    // first output row
     const int r1 = min(r0 + p.strip, p.out_row0 + p.out_rows);     // one past last
     const int u_first = r0 - 1;
@@ -841,7 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         // Zero this quadrant's lanes of every accumulator column.
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
         const uint32_t zeros[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int c = 0; c < p.ntile * p.n_mb * N; c += 8) tmem_st8(lane_base + c, zeros);
+        for (int c = 0; c < NT * p.n_mb * N; c += 8) tmem_st8(lane_base + c, zeros);
         tmem_wait_st();
     }
     fence_before_sync();
@@ -871,9 +878,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             // them ~0.3-0.5 us apart (measured).
             for (int grp = 0; grp < p.n_grp && ok; ++grp) {
             // Two tiles: group = tile, every M-block; one tile: M-block ranges.
-            const int tile = p.ntile == 2 ? grp : 0;
-            const int m_beg = p.ntile == 2 ? 0 : grp * p.grp_size;
-            const int m_end = p.ntile == 2 ? p.n_mb : min(p.n_mb, m_beg + p.grp_size);
+            const int tile = NT == 2 ? grp : 0;
+            const int m_beg = NT == 2 ? 0 : grp * p.grp_size;
+            const int m_end = NT == 2 ? p.n_mb : min(p.n_mb, m_beg + p.grp_size);
             const int w0t = w0 + kWt * tile;  // the tile's first column
             const int w = w0t + (rr & 7);
             const uint32_t tile_cols = static_cast<uint32_t>(tile * p.n_mb * N);
@@ -999,9 +1006,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     }
                     fence_after_sync();
                     if (u >= 0 && u < p.H) {  // rows outside the image issue nothing
-                        const int tile = p.ntile == 2 ? grp : 0;
-                        const int m0 = p.ntile == 2 ? 0 : grp * p.grp_size;
-                        const int cnt = p.ntile == 2 ? p.n_mb : min(p.grp_size, p.n_mb - m0);
+                        const int tile = NT == 2 ? grp : 0;
+                        const int m0 = NT == 2 ? 0 : grp * p.grp_size;
+                        const int cnt = NT == 2 ? p.n_mb : min(p.grp_size, p.n_mb - m0);
                         const int rot = (((1 - u) % 3) + 3) % 3;
                         const uint64_t a0 = vol_base + static_cast<uint64_t>((vb * p.vol_buf_bytes) >> 4) +
                                             static_cast<uint64_t>((tile * p.tile_vol_bytes) >> 4) +
@@ -1051,11 +1058,11 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     const int g = kg * 8 + ge;
                     const bool gv = g < p.G;
                     const int64_t roff = ((i64(b) * p.C + (gv ? g * Cg + cc : 0)) * p.in_rows + urow) * p.W;
-                    const int nlv = p.l_stage_w / 8;
+                    constexpr int nlv = (kLStageW + kWt * (NT - 1)) / 8;
                     for (int v = 0; v < nlv + nvr; ++v) {
                         const bool isL = v < nlv;
                         const int x = isL ? (w0 - 8 + 8 * v) : (rbase + 8 * (v - nlv));
-                        const uint32_t dst = isL ? sbase + p.off_l + lc * p.l_row_bytes + 16 * v
+                        const uint32_t dst = isL ? sbase + p.off_l + lc * (2 * (kLStageW + kWt * (NT - 1))) + 16 * v
                                                  : rchunk(sbase + lc * 128u, lc, v - nlv, p.rbox_bytes);
                         const __half* srow = (isL ? p.left : p.right) + roff;
                         if (p.vec_ok) {
@@ -1168,12 +1175,12 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         // this warp's tasks of the job: tau = job * T + h with
                         // T = tpj * ntile tasks per job, tau % kProdWarps == pw;
                         // task h is range h % tpj of tile h / tpj.
-                        const int T = p.tpj * p.ntile;
+                        const int T = p.tpj * NT;
                         for (int h = ((pw - job * T) % kProdWarps + kProdWarps) % kProdWarps; h < T; h += kProdWarps) {
-                            const int tl = h / p.tpj, hh = h - tl * p.tpj;
+                            const int tl = NT == 2 ? h / p.tpj : 0, hh = h - tl * p.tpj;
                             const int jt0 = (hh * p.n_tiles) / p.tpj, jt1 = ((hh + 1) * p.n_tiles) / p.tpj;
-                            corr_task<CORR>(p, sbase, zero_row, vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes, jt0,
-                                            jt1, lane, tl);
+                            corr_task<CORR, NT>(p, sbase, zero_row, vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes,
+                                                jt0, jt1, lane, tl);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
@@ -1270,6 +1277,15 @@ int set_fused_corr_engine(int engine) noexcept
 int fused_corr_engine() noexcept
 {
     return g_corr_engine.load();
+}
+
+// The two-tile instantiation of a fused variant (Cout <= 16 and the
+// tensor-core correlation variants only; nullptr for the others).
+template <int CP, int CV>
+constexpr void (*dual_tile_kernel())(StemParams)
+{
+    if constexpr (CP == 16 && CV >= 1 && CV <= 4) return stem_tc_kernel<CP, true, CV, 2>;
+    else return nullptr;
 }
 
 // Whether the stem kernel takes a shape: WW_SUCCESS, WW_ERR_INVALID_SHAPE or
@@ -1499,11 +1515,11 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     using KernelFn = void (*)(StemParams);
     KernelFn kernel = nullptr;
     if (!fused) {
-        kernel = coutp == 16 ? stem_tc_kernel<16, false, 0> : stem_tc_kernel<32, false, 0>;
+        kernel = coutp == 16 ? stem_tc_kernel<16, false, 0, 1> : stem_tc_kernel<32, false, 0, 1>;
     } else {
         const int cv = corr_variant(Cg, cuda_core_corr);
 #define WW_FUSED_CASE(CP, CV) \
-    if (coutp == CP && cv == CV) kernel = stem_tc_kernel<CP, true, CV>;
+    if (coutp == CP && cv == CV) kernel = p.ntile == 2 ? dual_tile_kernel<CP, CV>() : stem_tc_kernel<CP, true, CV, 1>;
         WW_FUSED_CASE(16, 1) WW_FUSED_CASE(16, 2) WW_FUSED_CASE(16, 3) WW_FUSED_CASE(16, 4) WW_FUSED_CASE(16, 5)
         WW_FUSED_CASE(32, 1) WW_FUSED_CASE(32, 2) WW_FUSED_CASE(32, 3) WW_FUSED_CASE(32, 4) WW_FUSED_CASE(32, 5)
         WW_FUSED_CASE(16, 6) WW_FUSED_CASE(16, 7) WW_FUSED_CASE(16, 8) WW_FUSED_CASE(16, 9) WW_FUSED_CASE(16, 10)

@@ -90,6 +90,12 @@ constexpr int kProdWarps = 8;
 constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;  // 448
 constexpr int kMaxMB = 10;         // M-blocks per CTA (TMEM: kMaxMB * 3 * 16 <= 512)
 constexpr int kLStageW = 24;       // staged left columns [w0-8, w0+16)
+// Staged left columns with nt column tiles per CTA: [w0 - 8, w0 + 16) for
+// one tile; for two, [w0 - 8, w0 + 32), 40 rather than the 32 needed, so the
+// 80-byte rows keep the 8 channel rows of each transposing ldmatrix in
+// distinct 16-byte bank groups (64-byte rows: 4-way conflicts, measured
+// 3.6x the shared-memory bank conflicts).
+__host__ __device__ constexpr int lstage_w(int nt) { return nt == 2 ? 40 : kLStageW; }
 constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
@@ -351,7 +357,7 @@ template <int KM, bool FULL, int NT>
 __device__ __forceinline__ void corr_task_mma(const StemParams& p, uint32_t slot, uint32_t zero_row,
                                               uint32_t vsa, int jt0, int jt1, int lane, int tl)
 {
-    constexpr int LRB = 2 * (kLStageW + kWt * (NT - 1));  // staged left row bytes
+    constexpr int LRB = 2 * lstage_w(NT);  // staged left row bytes
     if constexpr (NT == 1) tl = 0;
     constexpr int NA = KM == 8 ? 2 : 4;  // A registers per group
     constexpr int NB = KM == 8 ? 1 : 2;  // B registers per group and tile
@@ -1058,11 +1064,11 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     const int g = kg * 8 + ge;
                     const bool gv = g < p.G;
                     const int64_t roff = ((i64(b) * p.C + (gv ? g * Cg + cc : 0)) * p.in_rows + urow) * p.W;
-                    constexpr int nlv = (kLStageW + kWt * (NT - 1)) / 8;
+                    constexpr int nlv = lstage_w(NT) / 8;
                     for (int v = 0; v < nlv + nvr; ++v) {
                         const bool isL = v < nlv;
                         const int x = isL ? (w0 - 8 + 8 * v) : (rbase + 8 * (v - nlv));
-                        const uint32_t dst = isL ? sbase + p.off_l + lc * (2 * (kLStageW + kWt * (NT - 1))) + 16 * v
+                        const uint32_t dst = isL ? sbase + p.off_l + lc * (2 * lstage_w(NT)) + 16 * v
                                                  : rchunk(sbase + lc * 128u, lc, v - nlv, p.rbox_bytes);
                         const __half* srow = (isL ? p.left : p.right) + roff;
                         if (p.vec_ok) {
@@ -1392,7 +1398,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     // buffers when three staging slots still fit.
     auto geometry = [&](int nt) -> size_t {
         p.ntile = nt;
-        p.l_stage_w = kLStageW + kWt * (nt - 1);    // left columns [w0 - 8, w0 + 8 nt + 8)
+        p.l_stage_w = lstage_w(nt);
         p.l_row_bytes = 2 * p.l_stage_w;
         p.n_wtiles = (W + kWt * nt - 1) / (kWt * nt);
         p.rstage_w = 16 + 8 * ((D + 7) / 8) + kWt * (nt - 1);  // right columns [w0 - 8 ceil(D/8), w0 + 8 nt + 8)

@@ -66,9 +66,9 @@ DEFAULT_CONFIG = 4
 # is captured at B = 8 and scaled by 64 / 8 (traffic is per pair).
 NCU_TRAFFIC_BYTES = {
     "c2_gwc40_stem32": 24.84e6 + 7.11e6,
-    "c3_hd_gwc8_stem16": 90.41e6 + 419.93e6,
+    "c3_hd_gwc8_stem16": 126.54e6 + 449.70e6,
     "c4_batched_gwc32_stem32": (274.21e6 + 687.38e6) * 8,
-    "c5_edge_gwc16_stem16": 6.40e6 + 0.001e6,
+    "c5_edge_gwc16_stem16": 6.56e6 + 0.17e6,
 }
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per chunk).

@@ -143,14 +143,17 @@ int ww_set_fused_corr_engine(int engine);
 int ww_get_fused_corr_engine(void);
 
 /* Limits of ww_corr_cost_stem3d / _band / _multi and of ww_cost_stem3d
- * (this build): Cout <= 32; D <= 80 when Cout > 16 and D <= 160 when
- * Cout <= 16 (three Cout-column tensor-memory accumulators per 16
- * disparities within 512 columns); G (or Cin) <= 56 (at most 32 K-steps of
- * two 8-group chunks); and the weights, two volume rows and two staging
- * slots within the device's shared memory, which bounds G further: on a
- * B200 with C / G = 8 the largest G is 48, 40, 32, 24 for Cout 17..32 and
- * D = 32, 48, 64, 80, and 56, 56, 40, 40, 32, 24, 16 for Cout <= 16 and
- * D = 32, 48, 64, 80, 96, 128, 160.  Shapes outside them return
+ * (this build): Cout <= 32; G (or Cin) <= 56 (at most 32 K-steps of two
+ * 8-group chunks); and the weights, two volume rows and two staging slots
+ * of a 16-disparity band within the device's shared memory, which bounds
+ * wide groups (on a B200 every G <= 56 fits with C / G = 8; G = 56 with
+ * C / G = 32 and Cout 17..32 does not).  Any D: a disparity range one
+ * launch cannot hold (three
+ * Cout-column tensor-memory accumulators per 16 disparities within 512
+ * columns, i.e. more than 80 disparities for Cout 17..32 or 160 for
+ * Cout <= 16, or a shared-memory layout that does not fit) runs as several
+ * launches over disparity bands, each with the volume plane below and above
+ * it, with the same result.  Shapes outside the limits return
  * WW_ERR_UNSUPPORTED.  These two functions answer without launching
  * anything (0, WW_ERR_INVALID_SHAPE or WW_ERR_UNSUPPORTED), using the current
  * device's shared memory, or a B200's when no usable device is current. */

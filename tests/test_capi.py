@@ -255,26 +255,30 @@ def test_configs_fold_matches_library(ww):
 
 
 def test_fused_limits_are_reported_and_enforced_at_build_time(ww):
-    """The limits in the header: Cout <= 32, D <= 80 (Cout > 16) or 160
-    (Cout <= 16), G <= 56 and shared memory (G <= 40 for Cout 32 at D = 48
-    on a B200); the plugin's output_dims refuses a shape outside them, so an
-    engine build fails instead of the enqueue."""
+    """The limits in the header: Cout <= 32, G <= 56 and shared memory for a
+    16-disparity band (wide groups: C / G = 32 with G = 56 does not fit); any
+    D (ranges one launch cannot hold run as disparity bands); the plugin's
+    output_dims refuses a shape outside them, so an engine build fails
+    instead of the enqueue."""
     L = ww.lib()
     for C, G, D, Cout in ((320, 40, 48, 32), (96, 8, 64, 16), (256, 32, 48, 32), (64, 16, 32, 16),
-                          (64, 8, 80, 32), (32, 8, 160, 16), (448, 56, 48, 16), (320, 40, 48, 32)):
+                          (64, 8, 80, 32), (32, 8, 160, 16), (448, 56, 48, 16), (320, 40, 48, 32),
+                          (64, 8, 81, 32), (32, 8, 161, 16), (64, 8, 192, 32), (96, 8, 400, 16)):
         assert L.ww_corr_cost_stem3d_supported(C, G, D, Cout) == 0, (C, G, D, Cout)
-    assert L.ww_corr_cost_stem3d_supported(64, 8, 81, 32) == 5    # D past 80 with Cout 32
-    assert L.ww_corr_cost_stem3d_supported(32, 8, 161, 16) == 5   # D past 160 with Cout 16
     assert L.ww_corr_cost_stem3d_supported(512, 64, 48, 16) == 5  # G past 56
-    assert L.ww_corr_cost_stem3d_supported(384, 48, 48, 32) == 5  # weights + volume rows past shared memory
+    assert L.ww_corr_cost_stem3d_supported(384, 48, 48, 32) == 0  # 16-disparity bands fit shared memory
+    assert L.ww_corr_cost_stem3d_supported(1792, 56, 48, 32) == 5  # 32-channel groups: staging past shared memory
     assert L.ww_corr_cost_stem3d_supported(64, 8, 48, 33) == 5    # Cout past 32
     assert L.ww_corr_cost_stem3d_supported(64, 6, 48, 32) == 2    # G does not divide C
     assert L.ww_cost_stem3d_supported(40, 48, 32) == 0
-    assert L.ww_cost_stem3d_supported(40, 96, 32) == 5
+    assert L.ww_cost_stem3d_supported(40, 96, 32) == 0   # two disparity bands
+    assert L.ww_cost_stem3d_supported(64, 48, 32) == 5   # Cin past 56
     out = Desc()
     ok = descs(desc([1, 64, 20, 40]), desc([1, 64, 20, 40]), desc([32, 8, 3, 3, 3]), desc([32]))
     assert L.ww_plugin_corr_cost_stem3d_output_dims(80, 8, 4, ok, ctypes.byref(out)) == 0
-    assert L.ww_plugin_corr_cost_stem3d_output_dims(96, 8, 4, ok, ctypes.byref(out)) == 1
+    assert L.ww_plugin_corr_cost_stem3d_output_dims(192, 8, 4, ok, ctypes.byref(out)) == 0  # disparity bands
+    wide = descs(desc([1, 56 * 32, 20, 40]), desc([1, 56 * 32, 20, 40]), desc([32, 56, 3, 3, 3]), desc([32]))
+    assert L.ww_plugin_corr_cost_stem3d_output_dims(48, 56, 4, wide, ctypes.byref(out)) == 1  # past shared memory
     assert L.ww_plugin_corr_cost_stem3d_output_dims(48, 4, 4, ok, ctypes.byref(out)) == 1   # weights' G != num_groups
     big = descs(desc([1, 64, 20, 40, 96]), desc([32, 64, 3, 3, 3]), desc([32]))
     assert L.ww_plugin_cost_stem3d_output_dims(3, big, ctypes.byref(out)) == 1

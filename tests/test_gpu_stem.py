@@ -201,6 +201,51 @@ def test_cuda_core_engine_full_size(ww, torch, orc, cuda_core_engine, cfg_id, B)
 
 
 @pytest.mark.parametrize("shape", [
+    # (B, C, G, H, W, D, Cout): disparity ranges that run as several bands
+    (1, 64, 8, 5, 40, 96, 32),    # bands of 80 + 16
+    (1, 32, 4, 4, 48, 192, 16),   # 160 + 32 (two column tiles per CTA)
+    (2, 64, 8, 3, 24, 200, 16),   # 160 + 40: D not a multiple of 16
+    (1, 40, 5, 4, 33, 120, 32),   # 80 + 40, odd W (cp.async staging), lone octet
+])
+def test_fused_disparity_bands(ww, torch, orc, shape):
+    """Disparity ranges that one launch cannot hold run as bands, each with
+    the volume plane below and above it: within the fp16 tolerance of the
+    oracle, and with the CUDA-core correlation bit-identical to
+    corr_volume -> cost_stem3d (the volume form runs the same bands)."""
+    from whirlwind_trt_plugins_b200.configs import FrontEnd, make_inputs
+    B, C, G, H, W, D, Cout = shape
+    cfg = FrontEnd("bands", B=B, C=C, G=G, H=H, W=W, D=D, Cout=Cout)
+    x = make_inputs(cfg, seed=D + W)
+    tl, tr, tw, tb = (_t(torch, x[k]) for k in ("left", "right", "w", "b"))
+    out = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+    ref = orc.corr_stem(x["left"], x["right"], x["w"], x["b"], cfg.D, cfg.G, acc_mode=orc.ACC_F64)
+    err = np.abs(out.cpu().numpy().astype(np.float32) - ref.astype(np.float32)).max()
+    assert err <= ATOL_F16, f"max abs err {err}"
+    prev = ww.set_fused_corr_engine(ww.CORR_ENGINE_CUDA_CORES)
+    try:
+        fused = ww.corr_cost_stem3d(tl, tr, tw, tb, cfg.D, cfg.G)
+        unfused = ww.cost_stem3d(ww.corr_volume(tl, tr, cfg.D, cfg.G), tw, tb)
+    finally:
+        ww.set_fused_corr_engine(prev)
+    assert torch.equal(fused, unfused)
+    assert ww.device_error() == 0
+
+
+def test_stem_disparity_bands_volume_form(ww, torch, orc):
+    """The generalised stem on a 96-disparity volume with Cout = 32 (two
+    bands) against the oracle's conv3d."""
+    rng = np.random.default_rng(96)
+    B, Cin, D, H, W, Cout = 1, 16, 96, 4, 24, 32
+    vol = (rng.standard_normal((B, Cin, D, H, W)) * 0.5).astype(np.float16)
+    w = (rng.standard_normal((Cout, Cin, 3, 3, 3)) * 0.05).astype(np.float16)
+    b = (rng.standard_normal(Cout) * 0.1).astype(np.float16)
+    out = ww.cost_stem3d(_t(torch, vol), _t(torch, w), _t(torch, b)).cpu().numpy().astype(np.float32)
+    ref = orc.stem(vol, w, b, acc_mode=orc.ACC_F64).astype(np.float32)
+    assert float(np.abs(out - ref).max()) <= ATOL_F16
+    assert ww.device_error() == 0
+
+
+@pytest.mark.parametrize("shape", [
     # (B, C, G, H, W, D, Cout): channel widths on every correlation path
     (1, 64, 2, 5, 24, 24, 16),     # Cg = 32: channels in two tensor-core chunks
     (1, 40, 2, 4, 20, 20, 8),      # Cg = 20 (zero-padded chunk), W % 8 != 0 (scalar staging)

@@ -119,7 +119,10 @@ struct StemParams {
     const __half* bias;   // [Cout]
     __half* out;          // [B, Cout, D, out_rows, W]
     int* err;
-    int B, C, G, H, W, D, Cout, act;
+    int B, C, G, H, W, D, Cout, act;   // D: disparities of this launch's band
+    int d_off, D_tot;         // band start, disparities of the whole volume (output [B, Cout, D_tot, ...])
+    int d_lo, d_hi;           // band-relative disparities whose volume planes are filled: [-1 or 0, D or D + 1)
+    int n8;                   // right-column runs of 8 staged per job: ceil(d_hi / 8)
     int in_row0, in_rows, out_row0, out_rows;
     int Cg, KG, Dp, n_mb, nsteps, strip, n_strips, n_wtiles;
     float inv_cg;
@@ -307,7 +310,7 @@ __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float
     for (int i = 0; i < 4; ++i) {
         const int wp = tile_row_wp(m + 8 * (i >> 1));
         const int d = dbase + wp - (8 * jt + 2 * q + ((i & 1) ^ (flip ? 1 : 0)));
-        if (wp < kWtp && d >= 0 && d < p.D) {
+        if (wp < kWtp && d >= p.d_lo && d < p.d_hi) {
             uint32_t h[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -608,7 +611,7 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int d = d0 - j;
-        if (full || (d >= 0 && d < p.D)) {
+        if (full || (d >= p.d_lo && d < p.d_hi)) {
             uint2 v;
             if (p.scale_div) {
                 const float cg = static_cast<float>(Cg);
@@ -759,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     // slot j % n_slots: one elected lane arms stage_full with the byte count
     // and issues n_rbox right boxes and one left box (zero fill outside the
     // image and past the last channel).
-    const int n_runs = (p.D + 7) / 8;
+    const int n_runs = p.n8;
     auto tma_job = [&](int j) {
         const int slot = j % p.n_slots;
         const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
@@ -768,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         const uint32_t full = smem_addr(&stage_full[slot]);
         mbar_arrive_expect_tx(full, p.stage_tx);
         for (int k = 0; k < p.n_rbox; ++k)
-            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs + 64 * k, urow, c0, b, full);
+            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs - p.d_off + 64 * k, urow, c0, b, full);
         tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, c0, b, full);
     };
     // The first n_slots jobs need no free slot: issue them now, so their
@@ -873,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         const int dsub = rr >> 3;         // 0..15
         const float* sbias = reinterpret_cast<const float*>(smem + p.off_bias);
         const int64_t plane_out = i64(p.out_rows) * p.W;
-        const int64_t ostride = i64(p.D) * plane_out;
+        const int64_t ostride = i64(p.D_tot) * plane_out;
         bool ok = true;
         for (int it = 0; it < n_iter && ok; ++it) {
             const int r = u_first + it - 1;  // output row completed by this volume row
@@ -943,7 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     }
                 }
                 if (!ok || r < r0 || r >= r1) continue;  // warp-uniform
-                __half* orow0 = p.out + (i64(b) * p.Cout * p.D) * plane_out + i64(r - p.out_row0) * p.W;
+                __half* orow0 = p.out + (i64(b) * p.Cout * p.D_tot + p.d_off) * plane_out + i64(r - p.out_row0) * p.W;
 #pragma unroll
                 for (int j = 0; j < kDrain; ++j) {
                     if (j >= mcnt) break;
@@ -1043,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         if (FUSED) {
             const int Cg = p.Cg;
             const int NS = p.n_slots;
-            const int rbase = w0 - 8 * n_runs;
+            const int rbase = w0 - 8 * n_runs - p.d_off;
             const int nvr = p.rstage_w / 8;
             int issued = n_pre;  // jobs [0, n_pre) were issued during set-up
             for (int j = n_pre; j < total_jobs; ++j) {
@@ -1195,16 +1198,16 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     for (int kg = 0; kg < p.KG; ++kg) {
                         // Volume mode: gather vol[b, g, d, u, w] into the octet's rows.
                         const int64_t plane = i64(p.H) * p.W;
-                        for (int i = pw * 32 + lane; i < 8 * p.D * kWtp; i += kProdWarps * 32) {
+                        for (int i = pw * 32 + lane; i < 8 * (p.d_hi - p.d_lo) * kWtp; i += kProdWarps * 32) {
                             const int ge = i % 8;
                             const int rest = i / 8;
                             const int wp = rest % kWtp;
-                            const int d = rest / kWtp;
+                            const int d = p.d_lo + rest / kWtp;  // band-relative; plane d + 1
                             const int g = kg * 8 + ge;
                             const int wa = w0 - 1 + wp;
                             __half v = __float2half_rn(0.0f);
                             if (g < p.G && wa >= 0 && wa < p.W)
-                                v = p.vol[((i64(b) * p.G + g) * p.D + d) * plane + i64(u) * p.W + wa];
+                                v = p.vol[((i64(b) * p.G + g) * p.D_tot + p.d_off + d) * plane + i64(u) * p.W + wa];
                             *(reinterpret_cast<__half*>(vbuf + kg * p.lbo_vol + ((d + 1) * kWtp + wp) * 16) + ge) = v;
                         }
                     }
@@ -1294,26 +1297,23 @@ constexpr void (*dual_tile_kernel())(StemParams)
     else return nullptr;
 }
 
-// Whether the stem kernel takes a shape: WW_SUCCESS, WW_ERR_INVALID_SHAPE or
-// WW_ERR_UNSUPPORTED (the limits of this build: Cout <= 32; the stem's
-// accumulators -- three Cout-column slots per 16-disparity M-block -- within
-// the 512 tensor-memory columns, i.e. D <= 80 for Cout 17..32 and D <= 160
-// for Cout <= 16; at most kMaxSteps K-steps, i.e. G <= 56; and the smallest
-// shared-memory layout -- B image, two volume-row buffers, two staging slots
-// -- within smem_optin bytes).  fused: the correlation feeds the stem (C
-// channels in G groups); otherwise a G-channel volume is read.
-int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept
+namespace {
+
+// Whether one launch takes a band of Db disparities (halo: the band has a
+// volume plane above it, which widens the staged right window by one
+// disparity): the stem's accumulators -- three Cout-column slots per
+// 16-disparity M-block -- within the 512 tensor-memory columns, at most
+// kMaxSteps K-steps (G <= 56), and the smallest shared-memory layout -- B
+// image, two volume-row buffers, two staging slots -- within smem_optin.
+bool band_fits(bool fused, int C, int G, int Db, int Cout, int smem_optin, bool halo) noexcept
 {
-    if (C <= 0 || G <= 0 || D <= 0 || Cout <= 0) return WW_ERR_INVALID_SHAPE;
-    if (fused && C % G != 0) return WW_ERR_INVALID_SHAPE;
-    if (Cout > 32) return WW_ERR_UNSUPPORTED;
     const int coutp = Cout <= 16 ? 16 : 32;
     const int KG = (G + 7) / 8;
-    const int Dp = (D + 15) / 16 * 16;
+    const int Dp = (Db + 15) / 16 * 16;
     const int n_mb = Dp / 16;
-    if (n_mb * 3 * coutp > 512 || n_mb > kMaxMB) return WW_ERR_UNSUPPORTED;
+    if (n_mb * 3 * coutp > 512 || n_mb > kMaxMB) return false;
     const int nsteps = 9 * (KG / 2) + ((KG & 1) ? 5 : 0);
-    if (nsteps > kMaxSteps) return WW_ERR_UNSUPPORTED;
+    if (nsteps > kMaxSteps) return false;
     const long long Cg = fused ? C / G : 1;
     const long long vol_buf = static_cast<long long>(Dp + 2) * kWtp * 16 * KG + 128;
     long long o = static_cast<long long>(nsteps) * 2 * 5 * coutp * 16;
@@ -1325,40 +1325,52 @@ int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexc
     o += coutp * 4;
     o = (o + 1023) & ~1023LL;
     if (fused) {
-        const long long rstage_w = 16 + 8 * ((D + 7) / 8);
+        const long long rstage_w = 16 + 8 * ((Db + (halo ? 1 : 0) + 7) / 8);
         const long long n_rbox = (rstage_w + 63) / 64;
         const long long slot = ((n_rbox * 8 * Cg * 128 + 8 * Cg * kLRowBytes + 1023) / 1024) * 1024;
         o += 2 * slot;
     }
-    return o <= smem_optin ? WW_SUCCESS : WW_ERR_UNSUPPORTED;
+    return o <= smem_optin;
 }
 
-int stem_tc_launch(const void* vol, const void* left, const void* right, const void* w, const void* b,
-                   void* out, int B, int C, int G, int H, int W, int D, int Cout, int act, int in_row0,
-                   int in_rows, int out_row0, int out_rows, cudaStream_t stream) noexcept
+// Disparities per launch for a D-disparity volume: D when one launch takes
+// it, else the largest multiple of 16 that a band (with its halo planes)
+// fits; 0 when not even a 16-disparity band fits.
+int max_band(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept
+{
+    if (band_fits(fused, C, G, D, Cout, smem_optin, false)) return D;
+    for (int Db = (D - 1) / 16 * 16; Db >= 16; Db -= 16)
+        if (band_fits(fused, C, G, Db, Cout, smem_optin, true)) return Db;
+    return 0;
+}
+
+}  // namespace
+
+// Whether the stem kernel takes a shape: WW_SUCCESS, WW_ERR_INVALID_SHAPE or
+// WW_ERR_UNSUPPORTED.  The limits of this build: Cout <= 32; G <= 56 (at
+// most kMaxSteps K-steps); and a band of 16 disparities (or all of them when
+// fewer) must fit shared memory -- B image, two volume-row buffers, two
+// staging slots -- which bounds G further.  Any D is taken: disparity ranges
+// that one launch cannot hold run as several bands (stem_tc_launch).
+// fused: the correlation feeds the stem (C channels in G groups); otherwise a
+// G-channel volume is read.
+int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept
+{
+    if (C <= 0 || G <= 0 || D <= 0 || Cout <= 0) return WW_ERR_INVALID_SHAPE;
+    if (fused && C % G != 0) return WW_ERR_INVALID_SHAPE;
+    if (Cout > 32) return WW_ERR_UNSUPPORTED;
+    return max_band(fused, C, G, D, Cout, smem_optin) > 0 ? WW_SUCCESS : WW_ERR_UNSUPPORTED;
+}
+
+namespace {
+
+// One launch over disparities [d_off, d_off + D) of a D_tot-disparity volume.
+int stem_tc_launch_band(const void* vol, const void* left, const void* right, const void* w, const void* b,
+                        void* out, int B, int C, int G, int H, int W, int D_tot, int d_off, int D, int Cout, int act,
+                        int in_row0, int in_rows, int out_row0, int out_rows, cudaStream_t stream,
+                        const DeviceInfo& dev) noexcept
 {
     const bool fused = (vol == nullptr);
-    if (w == nullptr || b == nullptr || out == nullptr) return WW_ERR_NULL_POINTER;
-    if (B < 0 || C <= 0 || G <= 0 || H < 0 || W < 0 || D < 0 || Cout <= 0) return WW_ERR_INVALID_SHAPE;
-    if (fused && C % G != 0) return WW_ERR_INVALID_SHAPE;
-    if (act != WW_ACT_RELU && act != WW_ACT_RELU6) return WW_ERR_INVALID_SHAPE;
-    if (out_rows < 0 || out_row0 < 0 || out_row0 + out_rows > H) return WW_ERR_INVALID_SHAPE;
-    if (in_rows < 0 || in_row0 < 0 || in_row0 + in_rows > H) return WW_ERR_INVALID_SHAPE;
-    if (out_rows > 0) {
-        // the input band must hold rows [out_row0-1, out_row0+out_rows+1) clipped to [0,H)
-        const int need0 = out_row0 > 0 ? out_row0 - 1 : 0;
-        const int need1 = out_row0 + out_rows < H ? out_row0 + out_rows + 1 : H;
-        if (in_row0 > need0 || in_row0 + in_rows < need1) return WW_ERR_INVALID_SHAPE;
-    }
-    if (B == 0 || W == 0 || D == 0 || out_rows == 0) return WW_SUCCESS;
-    if (Cout > 32) return WW_ERR_UNSUPPORTED;
-
-    DeviceInfo dev;
-    if (current_device_info(&dev) != WW_SUCCESS || dev.cc_major < 10) return WW_ERR_DEVICE;
-    {
-        const int lim = stem_limits(fused, C, G, D, Cout, dev.smem_optin);
-        if (lim != WW_SUCCESS) return lim;
-    }
 
     const int coutp = Cout <= 16 ? 16 : 32;
     const int KG = (G + 7) / 8;
@@ -1379,6 +1391,11 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     p.err = device_error_slot();
     if (p.err == nullptr) return WW_ERR_DEVICE;
     p.B = B; p.C = C; p.G = G; p.H = H; p.W = W; p.D = D; p.Cout = Cout; p.act = act;
+    p.d_off = d_off;
+    p.D_tot = D_tot;
+    p.d_lo = d_off > 0 ? -1 : 0;                // the plane below the band: real data, or the zero padding
+    p.d_hi = d_off + D < D_tot ? D + 1 : D;     // the plane above the band likewise
+    p.n8 = (p.d_hi + 7) / 8;
     p.in_row0 = in_row0; p.in_rows = in_rows; p.out_row0 = out_row0; p.out_rows = out_rows;
     p.Cg = Cg; p.KG = KG; p.Dp = Dp; p.n_mb = n_mb; p.nsteps = nsteps;
     // The fused correlation scales by * (1 / Cg): exactly / Cg when Cg is a
@@ -1401,14 +1418,14 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
         p.l_stage_w = lstage_w(nt);
         p.l_row_bytes = 2 * p.l_stage_w;
         p.n_wtiles = (W + kWt * nt - 1) / (kWt * nt);
-        p.rstage_w = 16 + 8 * ((D + 7) / 8) + kWt * (nt - 1);  // right columns [w0 - 8 ceil(D/8), w0 + 8 nt + 8)
+        p.rstage_w = 16 + 8 * p.n8 + kWt * (nt - 1);  // right columns [w0 - d_off - 8 n8, w0 - d_off + 8 nt + 8)
         p.tmem_cols = pow2_cols(static_cast<uint32_t>(nt * n_mb * 3 * coutp));
         p.lbo_vol = static_cast<uint32_t>((Dp + 2) * kWtp * 16);
         // + a zeroed 128-byte guard per tile: the zero-weight partner of a lone
         // octet (step_info, t1 < 0) reads one 16-byte position past the last plane.
         p.tile_vol_bytes = p.lbo_vol * KG + 128;
         p.vol_buf_bytes = static_cast<uint32_t>(nt) * p.tile_vol_bytes;
-        p.n_tiles = (D + 7) / 8 + 2;
+        p.n_tiles = p.n8 + 2;
         p.n_rbox = (p.rstage_w + 63) / 64;
         p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
         p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
@@ -1478,9 +1495,9 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
         for (int jt = 0; jt < p.n_tiles; ++jt)
             for (int wp = 0; wp < kWtp; ++wp) {
                 const int dmax = dbase + wp - 8 * jt, dmin = dmax - 7;
-                if (dmax < 0 || dmin > D - 1) continue;
+                if (dmax < p.d_lo || dmin > p.d_hi - 1) continue;
                 if (p.n_fitems >= kMaxFItems) return WW_ERR_UNSUPPORTED;
-                const bool full = dmin >= 0 && dmax <= D - 1;
+                const bool full = dmin >= p.d_lo && dmax <= p.d_hi - 1;
                 p.fitems[p.n_fitems++] = static_cast<uint16_t>(wp | (jt << 4) | (full ? 0x8000 : 0));
             }
         const int per_job = 2 * p.n_fitems;  // two group halves per entry
@@ -1560,6 +1577,47 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
     if (grid > 0x7fffffffLL) return WW_ERR_UNSUPPORTED;
     kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
     return launch_status(op);
+}
+
+}  // namespace
+
+// Disparity bands: when the whole range does not fit one launch (tensor
+// memory holds three Cout-column accumulators per 16 disparities; shared
+// memory the weights, volume rows and staging), the volume is computed in
+// bands of the largest multiple of 16 disparities that fits, one launch each.
+// A band's volume buffer also holds the plane below and above it (real
+// correlation values, or the conv's zero padding at the ends), so every
+// output value sees exactly the taps it sees in one launch.
+int stem_tc_launch(const void* vol, const void* left, const void* right, const void* w, const void* b,
+                   void* out, int B, int C, int G, int H, int W, int D, int Cout, int act, int in_row0,
+                   int in_rows, int out_row0, int out_rows, cudaStream_t stream) noexcept
+{
+    const bool fused = (vol == nullptr);
+    if (w == nullptr || b == nullptr || out == nullptr) return WW_ERR_NULL_POINTER;
+    if (B < 0 || C <= 0 || G <= 0 || H < 0 || W < 0 || D < 0 || Cout <= 0) return WW_ERR_INVALID_SHAPE;
+    if (fused && C % G != 0) return WW_ERR_INVALID_SHAPE;
+    if (act != WW_ACT_RELU && act != WW_ACT_RELU6) return WW_ERR_INVALID_SHAPE;
+    if (out_rows < 0 || out_row0 < 0 || out_row0 + out_rows > H) return WW_ERR_INVALID_SHAPE;
+    if (in_rows < 0 || in_row0 < 0 || in_row0 + in_rows > H) return WW_ERR_INVALID_SHAPE;
+    if (out_rows > 0) {
+        // the input band must hold rows [out_row0-1, out_row0+out_rows+1) clipped to [0,H)
+        const int need0 = out_row0 > 0 ? out_row0 - 1 : 0;
+        const int need1 = out_row0 + out_rows < H ? out_row0 + out_rows + 1 : H;
+        if (in_row0 > need0 || in_row0 + in_rows < need1) return WW_ERR_INVALID_SHAPE;
+    }
+    if (B == 0 || W == 0 || D == 0 || out_rows == 0) return WW_SUCCESS;
+    if (Cout > 32) return WW_ERR_UNSUPPORTED;
+
+    DeviceInfo dev;
+    if (current_device_info(&dev) != WW_SUCCESS || dev.cc_major < 10) return WW_ERR_DEVICE;
+    const int band = max_band(fused, C, G, D, Cout, dev.smem_optin);
+    if (band <= 0) return stem_limits(fused, C, G, D, Cout, dev.smem_optin);
+    for (int d0 = 0; d0 < D; d0 += band) {
+        const int st = stem_tc_launch_band(vol, left, right, w, b, out, B, C, G, H, W, D, d0, std::min(band, D - d0),
+                                           Cout, act, in_row0, in_rows, out_row0, out_rows, stream, dev);
+        if (st != WW_SUCCESS) return st;
+    }
+    return WW_SUCCESS;
 }
 
 }  // namespace ww

@@ -41,6 +41,8 @@ constexpr int kVecW = 4;        // columns per thread
 constexpr int kDispPerThread = 8;
 constexpr int kChunkC = 16;     // channels staged per pass (32 with the narrow tiles)
 constexpr int kSmallOutputsPerSM = 800;  // below this many outputs per SM: one thread per output
+constexpr int kRuleDivide = 1;           // row-streaming kernels: scale by rounded division
+constexpr int kRuleZero = 2;             //   and an explicit +0 where w - d < 0 (the naive rule)
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -402,7 +404,7 @@ __device__ __forceinline__ uint32_t scale2_to_half2(float x, float y, float s)
 template <int CC, int CG>
 __global__ void __maxnreg__(64) corr_volume_rows_kernel(
     const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
-    int C, int H, int W, int D, int G, int rows, int tw, int scale_div, float inv_cg)
+    int C, int H, int W, int D, int G, int rows, int tw, int rule, float inv_cg)
 {
     constexpr int ND = kDispPerThread;
     const int DT = ND * blockDim.y;
@@ -425,9 +427,18 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
     const int dd0 = threadIdx.y * ND;
     const int rs = wl - dd0 + DT - ND;
     const int gx = w0 + wl;
-    // Every output of this thread has w >= d (no zero fill), all 8
-    // disparities exist, and all 4 columns are inside the image.
-    const bool plain = gx >= dd0 + ND - 1 && dd0 + ND <= D && gx + kVecW <= W && !scale_div;
+    // Packed epilogue when all 8 disparities exist, all 4 columns are inside
+    // the image, no division is needed and no output needs the naive rule's
+    // zero.  Under the fast rule the reference kernel
+    // (corr_volume_kernel.cu:220-228) writes acc * (1/C) for w - d < 0 too,
+    // from right columns staged as zeros: +0 for finite features, exactly
+    // what the zero-filled staging gives here, so those outputs need no test.
+    // Under the naive rule (:75-86) they are an explicit +0.
+    // rule: kRuleDivide (acc / Cg; otherwise * (1 / Cg), the same when Cg
+    // is a power of two) | kRuleZero (the naive rule's explicit +0).
+    const bool divide = (rule & kRuleDivide) != 0;
+    const bool zero_rule = (rule & kRuleZero) != 0;
+    const bool plain = dd0 + ND <= D && gx + kVecW <= W && !divide && !(zero_rule && gx < dd0 + ND - 1);
     __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
 
     auto stage = [&](int hh) {
@@ -489,8 +500,8 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
 #pragma unroll
                 for (int v = 0; v < kVecW; ++v) {
                     float val;
-                    if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
-                    else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
+                    else val = divide ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
                     tmp[v] = __float2half_rn(val);
                 }
                 __half* o = op + dd * plane;
@@ -515,7 +526,7 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
 template <int CC, int CG>
 __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
     const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
-    int C, int H, int W, int D, int G, int rows, int tw, int scale_div, float inv_cg)
+    int C, int H, int W, int D, int G, int rows, int tw, int rule, float inv_cg)
 {
     constexpr int ND = kDispPerThread;
     constexpr int VW = 8;
@@ -540,7 +551,9 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
     const int rs = wl - dd0 - ND + DT;  // 8-aligned: right value k (0..15) is column wl - dd0 - 8 + k
     const int gx = w0 + wl;
     const bool full_cols = gx + VW <= W;
-    const bool plain = gx >= dd0 + ND - 1 && dd0 + ND <= D && full_cols && !scale_div;
+    const bool divide = (rule & kRuleDivide) != 0;  // as in corr_volume_rows_kernel
+    const bool zero_rule = (rule & kRuleZero) != 0;
+    const bool plain = dd0 + ND <= D && full_cols && !divide && !(zero_rule && gx < dd0 + ND - 1);
     __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
 
     auto stage = [&](int hh) {
@@ -607,8 +620,8 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
 #pragma unroll
                 for (int v = 0; v < VW; ++v) {
                     float val;
-                    if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
-                    else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
+                    else val = divide ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
                     tmp[v] = __float2half_rn(val);
                 }
                 __half* o = op + dd * plane;
@@ -732,6 +745,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
     const bool is_half = dtype == WW_DTYPE_HALF;
     const int Cg = C / G;
     const int scale_div = corr_scale_div_grouped(is_half, B, C, G, H, W, D, dev.sm_count);
+    const int rule = scale_div ? (kRuleZero | ((C / G) & (C / G - 1) ? kRuleDivide : 0)) : 0;
     const float inv_cg = 1.0f / static_cast<float>(Cg);
 
     const int64_t total = static_cast<int64_t>(B) * G * D * H * W;
@@ -794,7 +808,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             dim3 block(tx8, ny8);
             dim3 grid(nt, (H + best - 1) / best, B * G);
             kern<<<grid, block, rsmem, stream>>>(static_cast<const __half*>(left), static_cast<const __half*>(right),
-                                                 static_cast<__half*>(out), C, H, W, D, G, best, tw, scale_div,
+                                                 static_cast<__half*>(out), C, H, W, D, G, best, tw, rule,
                                                  inv_cg);
             return launch_status("ww_corr_volume");
         }
@@ -827,7 +841,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             dim3 grid(nt, (H + best - 1) / best, B * G);
             kern<<<grid, block, rsmem, stream>>>(
                 static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out), C,
-                H, W, D, G, best, tw, scale_div, inv_cg);
+                H, W, D, G, best, tw, rule, inv_cg);
             return launch_status("ww_corr_volume");
         }
         dim3 block(tx, ny);

@@ -215,6 +215,13 @@ int ww_multi_split(int n, int H, int k, int* r0, int* r1, int* i0, int* i1);
  * disables.  The process-wide setting also affects concurrent callers. */
 int ww_multi_inject_copy_failure(int after_n_copies);
 
+/* Test hook: the naive CorrVolume rule divides every output by the group
+ * width (corr_volume_kernel.cu:84), computed here with one correction fma
+ * after a multiply by the rounded reciprocal (Markstein); this counts the
+ * fp32 values a, over all 2^32 bit patterns, for which that quotient differs
+ * from the IEEE rounded a / divisor (1 <= divisor <= 1024; synchronises). */
+int ww_selftest_int_division(int divisor, unsigned long long* mismatches);
+
 /* ---------------------------------------------------------------------------
  * CorrVolume (G = 1) fused with the reference's 3-stage CostStem3D, the pair
  * the reference runs at its native shape ([1, 1, 48, 32, 40]):

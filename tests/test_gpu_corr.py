@@ -149,3 +149,19 @@ def test_corr_rejects_bad_arguments(ww, torch):
     x = torch.zeros((1, 6, 2, 8), dtype=torch.float16, device=dev)
     with pytest.raises(ww.WWError):
         ww.corr_volume(x, x, 4, num_groups=4)
+
+
+def test_int_division_matches_rounded_division_on_every_float(ww):
+    """The naive rule's division by the group width is a multiply by the
+    rounded reciprocal plus one correction fma (Markstein); for every divisor
+    the library uses it for (1..1024) it equals the IEEE rounded division on
+    all 2^32 fp32 inputs, NaN payloads aside."""
+    import ctypes
+    L = ww.lib()
+    bad = {}
+    for b in range(1, 1025):
+        n = ctypes.c_ulonglong(0)
+        assert L.ww_selftest_int_division(b, ctypes.byref(n)) == 0
+        if n.value:
+            bad[b] = n.value
+    assert not bad, f"divisors with mismatches: {dict(list(bad.items())[:10])}"

@@ -93,6 +93,7 @@ def _load() -> ctypes.CDLL:
     L.ww_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.ww_clear_device_error.argtypes = []
     L.ww_set_fused_corr_engine.argtypes = [i]
+    L.ww_selftest_int_division.argtypes = [i, ctypes.POINTER(ctypes.c_ulonglong)]
     L.ww_get_fused_corr_engine.argtypes = []
     del f
     return L

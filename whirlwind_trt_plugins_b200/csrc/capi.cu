@@ -20,6 +20,7 @@ int stem_tc_launch(const void* vol, const void* left, const void* right, const v
                    cudaStream_t stream) noexcept;
 int stem_limits(bool fused, int C, int G, int D, int Cout, int smem_optin) noexcept;
 int set_fused_corr_engine(int engine) noexcept;
+int int_div_selftest(int b, unsigned long long* mismatches) noexcept;
 int fused_corr_engine() noexcept;
 int nv12_decode_launch(const void* nv12, void* out, int dtype, int B, int H_IN, int W_IN, int H_OUT,
                        int W_OUT, cudaStream_t stream) noexcept;
@@ -115,6 +116,11 @@ static int smem_optin_or_b200() noexcept
     if (ww::current_device_info(&d) == WW_SUCCESS) return d.smem_optin;
     cudaGetLastError();
     return 232448;
+}
+
+int ww_selftest_int_division(int divisor, unsigned long long* mismatches)
+{
+    return ww::int_div_selftest(divisor, mismatches);
 }
 
 int ww_set_fused_corr_engine(int engine)

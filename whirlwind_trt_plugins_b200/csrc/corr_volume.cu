@@ -29,6 +29,7 @@
 // 1 x 48 x 32 x 40 among them) run corr_volume_small_kernel instead: one
 // thread per output, operands through L2.
 
+#include "int_div.cuh"
 #include "ww_common.cuh"
 
 #include <type_traits>
@@ -209,7 +210,6 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
         __syncthreads();
     }
 
-    const float cg = static_cast<float>(Cg);
     T* obase = out + (i64(b) * G + g) * i64(D) * plane + i64(h) * W;
     const int gx = w0 + wl;
 #pragma unroll
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(256) corr_volume_kernel(
         for (int v = 0; v < kVecW; ++v) {
             float val;
             if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
-            else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+            else val = scale_div ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
             tmp[v] = from_f32<T>(val);
         }
         if (gx + kVecW <= W && (reinterpret_cast<uintptr_t>(op) % (kVecW * sizeof(T))) == 0) {
@@ -314,7 +314,6 @@ __global__ void __launch_bounds__(512) corr_volume_h_kernel(
         __syncthreads();
     }
 
-    const float cg = static_cast<float>(Cg);
     __half* obase = out + (i64(b) * G + g) * i64(D) * plane + i64(h) * W;
     const int gx = w0 + wl;
     if (gx >= W) return;
@@ -328,7 +327,7 @@ __global__ void __launch_bounds__(512) corr_volume_h_kernel(
         for (int v = 0; v < kVecW; ++v) {
             float val;
             if (gx + v < d) val = 0.0f;  // w - d < 0: exact +0
-            else val = scale_div ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+            else val = scale_div ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
             tmp[v] = __float2half_rn(val);
         }
         if (gx + kVecW <= W && (reinterpret_cast<uintptr_t>(op) % 8) == 0) {
@@ -491,7 +490,6 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
                 *reinterpret_cast<uint2*>(op + dd * plane) = u;
             }
         } else if (gx < W) {
-            const float cg = static_cast<float>(Cg);
 #pragma unroll
             for (int dd = 0; dd < ND; ++dd) {
                 const int d = dd0 + dd;
@@ -501,7 +499,7 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
                 for (int v = 0; v < kVecW; ++v) {
                     float val;
                     if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
-                    else val = divide ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    else val = divide ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
                     tmp[v] = __float2half_rn(val);
                 }
                 __half* o = op + dd * plane;
@@ -611,7 +609,6 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
                 *reinterpret_cast<uint4*>(op + dd * plane) = u;
             }
         } else if (gx < W) {
-            const float cg = static_cast<float>(Cg);
 #pragma unroll
             for (int dd = 0; dd < ND; ++dd) {
                 const int d = dd0 + dd;
@@ -621,7 +618,7 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
                 for (int v = 0; v < VW; ++v) {
                     float val;
                     if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
-                    else val = divide ? __fdiv_rn(acc[dd][v], cg) : __fmul_rn(acc[dd][v], inv_cg);
+                    else val = divide ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
                     tmp[v] = __float2half_rn(val);
                 }
                 __half* o = op + dd * plane;
@@ -674,12 +671,51 @@ __global__ void __launch_bounds__(256) corr_volume_small_kernel(
 #pragma unroll 8
         for (int c = 0; c < Cg; ++c, lp += plane, rp += plane)
             acc = __fmaf_rn(to_f32<T>(__ldg(lp)), to_f32<T>(__ldg(rp)), acc);
-        val = scale_div ? __fdiv_rn(acc, static_cast<float>(Cg)) : __fmul_rn(acc, inv_cg);
+        val = scale_div ? div_int(acc, Cg, inv_cg) : __fmul_rn(acc, inv_cg);
     }
     out[i] = from_f32<T>(val);
 }
 
 }  // namespace
+
+namespace {
+
+__device__ unsigned long long g_int_div_mismatch;
+
+// div_int against the rounded division on every fp32 bit pattern a (NaN
+// results compare equal to NaN).
+__global__ void __launch_bounds__(256) int_div_selftest_kernel(int b, float y)
+{
+    unsigned long long bad = 0;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
+        const float a = __uint_as_float(static_cast<uint32_t>(i));
+        const float q1 = div_int(a, b, y), q2 = __fdiv_rn(a, static_cast<float>(b));
+        const bool same = __float_as_uint(q1) == __float_as_uint(q2) || (isnan(q1) && isnan(q2));
+        bad += same ? 0u : 1u;
+    }
+    if (bad != 0) atomicAdd(&g_int_div_mismatch, bad);
+}
+
+}  // namespace
+
+// Test hook: the number of fp32 values a for which div_int(a, b, RN(1/b))
+// differs from the rounded division a / b (synchronises).
+int int_div_selftest(int b, unsigned long long* mismatches) noexcept
+{
+    if (mismatches == nullptr) return WW_ERR_NULL_POINTER;
+    if (b < 1 || b > kMaxIntDivisor) return WW_ERR_INVALID_SHAPE;
+    DeviceInfo dev;
+    if (current_device_info(&dev) != WW_SUCCESS) return WW_ERR_DEVICE;
+    const unsigned long long zero = 0;
+    if (cudaMemcpyToSymbol(g_int_div_mismatch, &zero, sizeof(zero)) != cudaSuccess) return launch_status("ww_selftest_int_division");
+    int_div_selftest_kernel<<<dev.sm_count * 8, 256>>>(b, 1.0f / static_cast<float>(b));
+    const int st = launch_status("ww_selftest_int_division");
+    if (st != WW_SUCCESS) return st;
+    if (cudaMemcpyFromSymbol(mismatches, g_int_div_mismatch, sizeof(*mismatches)) != cudaSuccess)
+        return launch_status("ww_selftest_int_division");
+    return WW_SUCCESS;
+}
 
 // Scale rule of the reference kernel that launchCorrVolume<T> would run for a
 // call with (B, C, H, W, D): 1 = naive kernel (acc / C), 0 = fast kernel

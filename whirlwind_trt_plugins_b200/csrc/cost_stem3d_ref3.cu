@@ -30,6 +30,7 @@
 // CTAs in one wave on 148 SMs): the 4 NX independent chains per thread are
 // what hides the fma and shared-memory latency.
 
+#include "int_div.cuh"
 #include "ww_common.cuh"
 
 namespace ww {
@@ -270,13 +271,12 @@ __global__ void __launch_bounds__(kThreads, CORR ? 2 : 4) cost_stem3d_ref3_kerne
             }
         }
         if (tid < kLTile) {
-            const float cf = static_cast<float>(p.C);
 #pragma unroll
             for (int z = 0; z < I_D; ++z) {
                 const int gd = od0 - 3 + z, gh = oh0 - 3 + y, gw = ow0 - 3 + x;
                 float v = 0.0f;
                 if (inside(gd, gh, gw, D, H, W) && gw >= gd) {
-                    const float sc = p.scale_div ? __fdiv_rn(acc[z], cf) : __fmul_rn(acc[z], p.inv_c);
+                    const float sc = p.scale_div ? div_int(acc[z], p.C, p.inv_c) : __fmul_rn(acc[z], p.inv_c);
                     v = __half2float(__float2half_rn(sc));
                 }
                 s_in[(z * I_H + y) * I_W + x] = v;

@@ -59,6 +59,10 @@ sys.path.insert(0, ROOT)
 METRIC = "cost voxels/s (B*D*H*W) corr+3D stem"
 UNIT = "voxels/s"
 DEFAULT_CONFIG = 4
+# The standalone CorrVolume line: config 2 (one 120 x 160 pair, 40 groups);
+# config 4's 5.8 GB volume per batch would need ~23 GB of pinned host buffers
+# for the end-to-end leg.
+CORR_VOLUME_CONFIG = 2
 
 # DRAM bytes (read + write) per launch of the fused kernel on the full
 # configuration, from ncu captures (profiles/stem_tc_fused_*.md).  Configs 2
@@ -92,11 +96,13 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=DEFAULT_CONFIG)
+    ap.add_argument("--config", type=int, default=None,
+                    help=f"configuration (default {DEFAULT_CONFIG}; --op corr_volume: {CORR_VOLUME_CONFIG})")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the configuration's batch (profiling captures of a smaller case)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["corr_cost_stem3d", "nv12_decode", "disparity_regression", "stem3_native"],
+    ap.add_argument("--op", choices=["corr_cost_stem3d", "corr_volume", "nv12_decode", "disparity_regression",
+                                     "stem3_native"],
                     default="corr_cost_stem3d")
     ap.add_argument("--corr-engine", choices=["tensor", "cuda_cores"], default="tensor",
                     help="correlation engine of the fused op (ww_set_fused_corr_engine)")
@@ -717,6 +723,136 @@ def bench_nv12(args):
     print(json.dumps(line), flush=True)
 
 
+def corr_volume_e2e(ww, torch, dev_set, cfg, n, stream) -> dict:
+    """CorrVolume end to end: pinned host features in, pinned host volume out,
+    copies inside the timed region, three streams."""
+    L0, R0, O0 = dev_set
+    k3 = range(3)
+    hl = [torch.empty(L0.shape, dtype=L0.dtype, pin_memory=True).copy_(L0) for _ in k3]
+    hr = [torch.empty(R0.shape, dtype=R0.dtype, pin_memory=True).copy_(R0) for _ in k3]
+    ho = [torch.empty(O0.shape, dtype=O0.dtype, pin_memory=True) for _ in k3]
+    dl, dr, do = [torch.empty_like(L0) for _ in k3], [torch.empty_like(R0) for _ in k3], [torch.empty_like(O0) for _ in k3]
+    strs = [torch.cuda.Stream() for _ in k3]
+
+    def one(i):
+        k = i % 3
+        with torch.cuda.stream(strs[k]):
+            dl[k].copy_(hl[k], non_blocking=True)
+            dr[k].copy_(hr[k], non_blocking=True)
+            ww.corr_volume(dl[k], dr[k], cfg.D, cfg.G, out=do[k], stream=strs[k])
+            ho[k].copy_(do[k], non_blocking=True)
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for st in strs:
+        st.wait_stream(stream)
+    for i in range(n):
+        one(i)
+    for st in strs:
+        stream.wait_stream(st)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    vals = cfg.B * cfg.G * cfg.D * cfg.H * cfg.W
+    return {"value": vals * n / (f0.elapsed_time(f1) * 1e-3), "unit": "values/s", "steps": n, "streams": 3}
+
+
+def corr_volume_cpu(dev_set, cfg) -> dict:
+    """The C oracle (the reference's fp32 channel-order sum and scale rule) on
+    all host threads over a bounded sample of image rows, scaled to values/s."""
+    import oracle
+    n = oracle.nthreads_default()
+    rows = max(1, min(cfg.H, 8))
+    L = dev_set[0][:1, :, :rows].cpu().numpy()
+    R = dev_set[1][:1, :, :rows].cpu().numpy()
+    mode = oracle.grouped_scale_mode(True, cfg.B, cfg.C, cfg.G, cfg.H, cfg.W, cfg.D)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < 5.0:
+        oracle.corr_f16(L, R, cfg.D, cfg.G, scale_mode=mode, nthreads=n)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": cfg.G * cfg.D * rows * cfg.W * reps / dt, "unit": "values/s", "cores": n, "kind": "port",
+            "sample": f"{reps} runs over rows [0,{rows}) of batch item 0 in the C oracle, {dt:.1f} s"}
+
+
+def bench_corr_volume(args):
+    """The reference's CorrVolume on a configuration's features (--config,
+    default 2), group-wise: one step = one ww_corr_volume launch.  value:
+    output values/s (B*G*D*H*W); roofline against HBM with bytes = both
+    feature maps read once + the fp16 volume written."""
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    C_ = load_configs()
+    cfg = C_.CONFIGS[args.config or CORR_VOLUME_CONFIG]
+    if args.batch:
+        cfg = cfg.scaled(B=args.batch)
+    torch.cuda.set_device(0)
+    B, C, G, H, W, D = cfg.B, cfg.C, cfg.G, cfg.H, cfg.W, cfg.D
+    in_bytes, out_bytes = 2 * B * C * H * W * 2, B * G * D * H * W * 2
+    n_sets = max(2, -(-400 * 2**20 // (in_bytes + out_bytes)))  # > 126 MB of L2
+    sets = []
+    for k in range(n_sets):
+        x = C_.make_inputs_torch(cfg, torch.device("cuda", 0), seed=11 + k)
+        sets.append((x["left"], x["right"], torch.empty((B, G, D, H, W), dtype=torch.float16, device="cuda")))
+    stream = torch.cuda.current_stream()
+
+    def step(i, st=None):
+        L, R, o = sets[i % n_sets]
+        ww.corr_volume(L, R, D, G, out=o, stream=st if st is not None else stream)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        print(f"profile run: corr_volume {cfg.name}, {max(3, args.warmup)} + {args.steps} launches", flush=True)
+        return
+    graph = torch.cuda.CUDAGraph()  # launches of ~30 us: time the kernels, not the Python launch path
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(args.steps):
+            step(i, torch.cuda.current_stream())
+    stream.wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    del graph
+    vals = B * G * D * H * W
+    e2e = corr_volume_e2e(ww, torch, sets[0], cfg, max(3, min(args.steps, 20)), stream)
+    e2e.update({"h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes})
+    peaks = load_peaks()
+    gbs = (in_bytes + out_bytes) / (ms * 1e-3) / 1e9
+    cpu = None if args.no_cpu_baseline else corr_volume_cpu(sets[0], cfg)
+    line = {
+        "metric": "corr volume values/s (B*G*D*H*W)", "value": vals / (ms * 1e-3), "unit": "values/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (the configuration's features)",
+        "config": {"workload": f"corr_volume {workload_name(cfg)}",
+                   "l2": f"{n_sets} rotating input/output sets > 126 MB L2",
+                   "timing": "the K launches replayed from one CUDA graph"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["src"]},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # Disparity regression workload: the aggregated cost of the batched config
 # (config 4: B = 64, D = 48, 94 x 312), fp16 in and out, soft-argmin.
 DISP_B, DISP_D, DISP_H, DISP_W = 64, 48, 94, 312
@@ -889,9 +1025,11 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.op != "corr_cost_stem3d":
         if rank == 0 and args.impl == "ours":
-            {"nv12_decode": bench_nv12, "disparity_regression": bench_disparity,
+            {"corr_volume": bench_corr_volume, "nv12_decode": bench_nv12, "disparity_regression": bench_disparity,
              "stem3_native": bench_stem3_native}[args.op](args)
         return
+    if args.config is None:
+        args.config = DEFAULT_CONFIG
     C = load_configs()
     cfg = C.CONFIGS[args.config]
     if cfg.Cout == 0:

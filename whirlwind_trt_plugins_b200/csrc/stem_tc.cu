@@ -132,9 +132,7 @@ struct StemParams {
     int n_slots;              // staging ring depth (2..kMaxSlots)
     int n_vbuf;               // volume row buffers (2..kMaxVBuf)
     int n_tiles;              // 8-column right tiles per job: ceil(D/8) + 2
-    int tpj;                  // producer tasks per job (each a range of the first n_tiles - 1 right tiles)
-    int n_corner;             // volume values of the last right tile (1 to 3; see corr_corner)
-    uint16_t corner[4];       // per value: w' | (x' - 8 (n_tiles - 1)) << 4 | (d + 1) << 8
+    int tpj;                  // producer tasks per job (each a range of right tiles)
     int raw_w_smem;           // weights staged through shared memory at set-up: 2 transposed, 1 as is, 0 not
     int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
     int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
@@ -628,35 +626,6 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
             *reinterpret_cast<uint2*>(row0 - j * kWtp * 16) = v;
         }
     }
-}
-
-// The last right tile of a job holds 1 to 3 volume values (the halo column
-// w' = 9 at disparity 0, and with a plane below the band w' = 8, 9 at -1):
-// a whole mma.sync tile per group for them was an eighth of the producers'
-// tensor work on configs 2 and 4.  Lane 8 k + e computes value k for group e
-// as an fp32 fma chain over the group's channels in order (products of fp16
-// values are exact) and stores it into the group's slot of its volume row.
-template <int NT>
-__device__ __forceinline__ void corr_corner(const StemParams& p, uint32_t slot, uint32_t vsa, int lane, int tl)
-{
-    constexpr int LRB = 2 * lstage_w(NT);
-    if constexpr (NT == 1) tl = 0;
-    const int k = lane >> 3, e = lane & 7;
-    if (k >= p.n_corner) return;
-    const int ent = p.corner[k];
-    const int wp = ent & 15, xo = (ent >> 4) & 7, dpl = ent >> 8;
-    const int jt = p.n_tiles - 1 + tl;  // staged right tile
-    const uint32_t lrow = slot + p.off_l + static_cast<uint32_t>(2 * (wp + 7 + 8 * tl));
-    float acc = 0.0f;
-    for (int c = 0; c < p.Cg; ++c) {
-        const int r = e * p.Cg + c;
-        const unsigned short rv = ld_shared_u16(rchunk(slot + static_cast<uint32_t>(r) * 128u, r, jt, p.rbox_bytes) +
-                                                static_cast<uint32_t>(2 * xo));
-        const unsigned short lv = ld_shared_u16(lrow + static_cast<uint32_t>(r * LRB));
-        acc = fma_f16f16f32(lv, rv, acc);
-    }
-    st_shared_u16(vsa + static_cast<uint32_t>((dpl * kWtp + wp) * 16 + 2 * e),
-                  __half_as_ushort(__float2half_rn(__fmul_rn(acc, p.inv_cg))));
 }
 
 // Correlation variants (a kernel template parameter, so each instantiation
@@ -1218,11 +1187,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         const int T = p.tpj * NT;
                         for (int h = ((pw - job * T) % kProdWarps + kProdWarps) % kProdWarps; h < T; h += kProdWarps) {
                             const int tl = NT == 2 ? h / p.tpj : 0, hh = h - tl * p.tpj;
-                            const int nmt = p.n_tiles - 1;  // mma.sync tiles; the last one is corr_corner's
-                            const int jt0 = (hh * nmt) / p.tpj, jt1 = ((hh + 1) * nmt) / p.tpj;
-                            const uint32_t vt = vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes;
-                            corr_task<CORR, NT>(p, sbase, zero_row, vt, jt0, jt1, lane, tl);
-                            if (hh == p.tpj - 1) corr_corner<NT>(p, sbase, vt, lane, tl);
+                            const int jt0 = (hh * p.n_tiles) / p.tpj, jt1 = ((hh + 1) * p.n_tiles) / p.tpj;
+                            corr_task<CORR, NT>(p, sbase, zero_row, vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes,
+                                                jt0, jt1, lane, tl);
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
@@ -1515,16 +1482,7 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
     // loads, while half the producer warps per job still keep a job's latency
     // (and so the staging ring's turnover) short (measured: 7 % faster than
     // one tile per task on config 2, and faster on every config).
-    p.tpj = p.n_tiles / 2;  // two of the first n_tiles - 1 right tiles per task
-    // The last right tile's values (corr_corner).
-    p.n_corner = 0;
-    for (int xo = 0; xo < 8; ++xo)
-        for (int wp = 0; wp < kWtp; ++wp) {
-            const int d = 8 * p.n8 - 1 + wp - (8 * (p.n_tiles - 1) + xo);
-            if (d < p.d_lo || d >= p.d_hi) continue;
-            if (p.n_corner >= 4) return WW_ERR_UNSUPPORTED;
-            p.corner[p.n_corner++] = static_cast<uint16_t>(wp | (xo << 4) | ((d + 1) << 8));
-        }
+    p.tpj = (p.n_tiles + 1) / 2;
     // CUDA-core correlation items: (right tile, volume column) pairs with
     // any disparity in [0, D), and the most jobs a task of 32 items touches.
     p.n_fitems = 0;

@@ -107,6 +107,30 @@ def test_stem_tc_matches_oracle(ww, torch, orc, case, act):
     assert np.all(np.isfinite(out))
 
 
+@pytest.mark.parametrize("case", [
+    dict(B=2, Cin=40, Cout=32, D=48, H=6, W=40),
+    dict(B=1, Cin=12, Cout=16, D=64, H=5, W=32),     # a partial octet
+    dict(B=1, Cin=8, Cout=16, D=200, H=3, W=16),     # disparity bands
+])
+def test_stem_volume_gather_paths_agree(ww, torch, case):
+    """The volume form's two gathers -- 16-byte loads with a register
+    transpose (W % 8 == 0, 16-byte aligned volume) and 2-byte loads (any
+    other volume) -- fill the same volume rows, so the outputs are equal bit
+    for bit; the 2-byte path is reached by passing a volume that starts one
+    element into its storage."""
+    B, Cin, Cout, D, H, W = (case[k] for k in ("B", "Cin", "Cout", "D", "H", "W"))
+    g = torch.Generator().manual_seed(Cin + D)
+    n = B * Cin * D * H * W
+    flat = (torch.randn(n + 8, generator=g) * 0.5).half().cuda()
+    shifted = flat[1:n + 1].view(B, Cin, D, H, W)
+    aligned = shifted.clone()
+    assert aligned.data_ptr() % 16 == 0 and shifted.data_ptr() % 16 != 0
+    w = (torch.randn(Cout, Cin, 3, 3, 3, generator=g) * 0.05).half().cuda()
+    b = (torch.randn(Cout, generator=g) * 0.1).half().cuda()
+    assert torch.equal(ww.cost_stem3d(aligned, w, b), ww.cost_stem3d(shifted, w, b))
+    assert ww.device_error() == 0
+
+
 # ------------------------------------------------------------ fused front end
 
 def _fused(ww, torch, x, cfg, act=0):

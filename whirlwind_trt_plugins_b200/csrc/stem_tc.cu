@@ -167,6 +167,8 @@ struct StemParams {
     uint16_t fitems[kMaxFItems];
     // TMA maps of the left / right features (4-D: x = W, y = row, z = channel,
     // w = batch); boxes [24] x [8 Cg] (left) and [64] x [8 Cg] (right, swizzled).
+    // Volume mode: tmap_l maps the volume (5-D, encode_volume_map), boxes
+    // [24 columns] x [planes] x [8 groups].
     CUtensorMap tmap_l;
     CUtensorMap tmap_r;
 };
@@ -692,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     // volume rows inside the image (a contiguous range) and the staging jobs over them
     const int uv0 = max(u_first, 0);
     const int uv1 = min(u_first + n_iter, p.H);
-    const int total_jobs = FUSED ? max(0, uv1 - uv0) * p.KG : 0;
+    const int total_jobs = (FUSED || p.use_tma) ? max(0, uv1 - uv0) * p.KG : 0;
 
     uint8_t* sB = smem + p.off_b;
     uint8_t* sVol = smem + p.off_vol;
@@ -761,23 +763,30 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     // TMA staging of job j (volume row uv0 + j / KG, group octet j % KG) into
     // slot j % n_slots: one elected lane arms stage_full with the byte count
     // and issues n_rbox right boxes and one left box (zero fill outside the
-    // image and past the last channel).
+    // image and past the last channel).  Volume mode: one box of the volume,
+    // [8 groups][planes d_lo .. d_hi - 1][columns w0 - 8 .. w0 + 15] (zero
+    // fill outside the image and past the last group).
     const int n_runs = p.n8;
     auto tma_job = [&](int j) {
         const int slot = j % p.n_slots;
         const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
-        const int urow = uv0 + j / p.KG - p.in_row0;
-        const int c0 = (j % p.KG) * 8 * p.Cg;
         const uint32_t full = smem_addr(&stage_full[slot]);
         mbar_arrive_expect_tx(full, p.stage_tx);
-        for (int k = 0; k < p.n_rbox; ++k)
-            tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs - p.d_off + 64 * k, urow, c0, b, full);
-        tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, c0, b, full);
+        if constexpr (FUSED) {
+            const int urow = uv0 + j / p.KG - p.in_row0;
+            const int c0 = (j % p.KG) * 8 * p.Cg;
+            for (int k = 0; k < p.n_rbox; ++k)
+                tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs - p.d_off + 64 * k, urow, c0, b,
+                            full);
+            tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, c0, b, full);
+        } else {
+            tma_load_5d(sbase, &p.tmap_l, w0 - 8, uv0 + j / p.KG, p.d_off + p.d_lo, 8 * (j % p.KG), b, full);
+        }
     };
     // The first n_slots jobs need no free slot: issue them now, so their
     // loads overlap the B image build (the staging ring is not touched by
     // set-up; the barriers are initialised and visible after the sync above).
-    const int n_pre = (FUSED && p.use_tma && wmode != 0) ? min(p.n_slots, total_jobs) : 0;
+    const int n_pre = (p.use_tma && wmode != 0) ? min(p.n_slots, total_jobs) : 0;
     if (n_pre > 0 && warp == kLoadWarp) {
         if (elect_one())
             for (int j = 0; j < n_pre; ++j) tma_job(j);
@@ -1043,7 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         // copies (zero fill outside the image and past the last channel).
         // Otherwise (W % 8 != 0 or unaligned features) lanes copy 16-byte
         // vectors of whole channel rows with cp.async (or element by element).
-        if (FUSED) {
+        if (FUSED || p.use_tma) {
             const int Cg = p.Cg;
             const int NS = p.n_slots;
             const int rbase = w0 - 8 * n_runs - p.d_off;
@@ -1058,6 +1067,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     __syncwarp();
                     continue;
                 }
+                if constexpr (!FUSED) continue;  // (volume mode stages only by TMA)
                 const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
                 const int urow = uv0 + j / p.KG - p.in_row0;
                 const int kg = j % p.KG;
@@ -1193,6 +1203,108 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
+                    }
+                } else if (p.use_tma) {
+                    // Volume mode, TMA-staged: job (u, octet kg) holds
+                    // [8 groups][np planes][24 columns w0 - 8 .. w0 + 15]; one
+                    // item per plane reads the 8 groups' interior columns as
+                    // 16-byte rows (lanes 48 bytes apart: no bank conflicts)
+                    // and the two halo columns, transposes in registers and
+                    // writes the octet's rows w' = 0..9 of the plane.  Items
+                    // of consecutive jobs start on different warps.
+                    const int np = p.d_hi - p.d_lo;
+                    const uint32_t gbytes = static_cast<uint32_t>(np) * 48u;
+                    const int job0 = (u - uv0) * p.KG;
+                    for (int kg = 0; kg < p.KG && ok; ++kg) {
+                        const int job = job0 + kg;
+                        const int slot = job % p.n_slots;
+                        if (!warp_wait(smem_addr(&stage_full[slot]), (job / p.n_slots) & 1, p.err, 7)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
+                        const uint32_t vrow0 = smem_addr(vbuf + kg * p.lbo_vol);
+                        int i = pw * 32 + lane - (job * np) % (kProdWarps * 32);
+                        if (i < 0) i += kProdWarps * 32;
+                        for (; i < np; i += kProdWarps * 32) {
+                            const uint32_t src = sbase + static_cast<uint32_t>(i) * 48u;
+                            uint32_t wg[8][4];
+                            unsigned short h0[8], h9[8];
+#pragma unroll
+                            for (int g = 0; g < 8; ++g) {
+                                ld_shared_v4(src + g * gbytes + 16u, wg[g]);
+                                h0[g] = ld_shared_u16(src + g * gbytes + 14u);
+                                h9[g] = ld_shared_u16(src + g * gbytes + 32u);
+                            }
+                            const uint32_t row = vrow0 + static_cast<uint32_t>((p.d_lo + i + 1) * kWtp * 16);
+                            st_shared_v4(row, pack_b16x2(h0[0], h0[1]), pack_b16x2(h0[2], h0[3]),
+                                         pack_b16x2(h0[4], h0[5]), pack_b16x2(h0[6], h0[7]));
+                            st_shared_v4(row + 9 * 16, pack_b16x2(h9[0], h9[1]), pack_b16x2(h9[2], h9[3]),
+                                         pack_b16x2(h9[4], h9[5]), pack_b16x2(h9[6], h9[7]));
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                st_shared_v4(row + (1 + 2 * k) * 16, __byte_perm(wg[0][k], wg[1][k], 0x5410),
+                                             __byte_perm(wg[2][k], wg[3][k], 0x5410),
+                                             __byte_perm(wg[4][k], wg[5][k], 0x5410),
+                                             __byte_perm(wg[6][k], wg[7][k], 0x5410));
+                                st_shared_v4(row + (2 + 2 * k) * 16, __byte_perm(wg[0][k], wg[1][k], 0x7632),
+                                             __byte_perm(wg[2][k], wg[3][k], 0x7632),
+                                             __byte_perm(wg[4][k], wg[5][k], 0x7632),
+                                             __byte_perm(wg[6][k], wg[7][k], 0x7632));
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_addr(&stage_empty[slot]));
+                    }
+                } else if (p.vec_ok) {
+                    // Volume mode, 16-byte path (W % 8 == 0, aligned volume):
+                    // one item per (octet, plane d) -- the 8 groups' interior
+                    // columns w0 .. w0 + 7 as one 16-byte load each, an 8 x 8
+                    // transpose in registers, and the two halo columns -- so
+                    // the octet's rows w' = 0..9 of plane d are written as ten
+                    // 16-byte rows.
+                    const int64_t plane = i64(p.H) * p.W;
+                    const int64_t gstride = i64(p.D_tot) * plane;
+                    const int nd = p.d_hi - p.d_lo;
+                    for (int i = pw * 32 + lane; i < p.KG * nd; i += kProdWarps * 32) {
+                        const int kg = i / nd;
+                        const int d = p.d_lo + (i - kg * nd);  // band-relative; plane d + 1
+                        const __half* src =
+                            p.vol + ((i64(b) * p.G + 8 * kg) * p.D_tot + p.d_off + d) * plane + i64(u) * p.W + w0;
+                        uint4 r[8];
+                        unsigned short h0[8], h9[8];
+#pragma unroll
+                        for (int g = 0; g < 8; ++g) {
+                            r[g] = make_uint4(0u, 0u, 0u, 0u);
+                            h0[g] = 0;
+                            h9[g] = 0;
+                            if (8 * kg + g < p.G) {
+                                const __half* s = src + g * gstride;
+                                r[g] = __ldg(reinterpret_cast<const uint4*>(s));
+                                if (w0 > 0) h0[g] = __half_as_ushort(__ldg(s - 1));
+                                if (w0 + 8 < p.W) h9[g] = __half_as_ushort(__ldg(s + 8));
+                            }
+                        }
+                        const uint32_t row = smem_addr(vbuf + kg * p.lbo_vol + (d + 1) * kWtp * 16);
+                        st_shared_v4(row, pack_b16x2(h0[0], h0[1]), pack_b16x2(h0[2], h0[3]), pack_b16x2(h0[4], h0[5]),
+                                     pack_b16x2(h0[6], h0[7]));
+                        st_shared_v4(row + 9 * 16, pack_b16x2(h9[0], h9[1]), pack_b16x2(h9[2], h9[3]),
+                                     pack_b16x2(h9[4], h9[5]), pack_b16x2(h9[6], h9[7]));
+                        // Column j of the interior is half j of every group's
+                        // load: word k of group g holds columns 2k, 2k + 1.
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            uint32_t wg[8];
+#pragma unroll
+                            for (int g = 0; g < 8; ++g)
+                                wg[g] = k == 0 ? r[g].x : (k == 1 ? r[g].y : (k == 2 ? r[g].z : r[g].w));
+                            st_shared_v4(row + (1 + 2 * k) * 16, __byte_perm(wg[0], wg[1], 0x5410),
+                                         __byte_perm(wg[2], wg[3], 0x5410), __byte_perm(wg[4], wg[5], 0x5410),
+                                         __byte_perm(wg[6], wg[7], 0x5410));
+                            st_shared_v4(row + (2 + 2 * k) * 16, __byte_perm(wg[0], wg[1], 0x7632),
+                                         __byte_perm(wg[2], wg[3], 0x7632), __byte_perm(wg[4], wg[5], 0x7632),
+                                         __byte_perm(wg[6], wg[7], 0x7632));
+                        }
                     }
                 } else {
                     for (int kg = 0; kg < p.KG; ++kg) {
@@ -1403,9 +1515,15 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
     // already differ from CorrVolume's fp32 chain at that level), and without
     // a division subroutine per value.
     p.inv_cg = 1.0f / static_cast<float>(Cg);
-    p.vec_ok = (W % 8 == 0) && (reinterpret_cast<uintptr_t>(left) % 16 == 0) &&
-               (reinterpret_cast<uintptr_t>(right) % 16 == 0);
+    // 16-byte loads: the features (fused) or the volume (volume mode).
+    p.vec_ok = (W % 8 == 0) && (fused ? (reinterpret_cast<uintptr_t>(left) % 16 == 0 &&
+                                         reinterpret_cast<uintptr_t>(right) % 16 == 0)
+                                      : reinterpret_cast<uintptr_t>(vol) % 16 == 0);
     const bool cuda_core_corr = fused && g_corr_engine.load(std::memory_order_relaxed) == WW_CORR_ENGINE_CUDA_CORES;
+    // Volume mode stages [8 groups][planes][24 columns] boxes by TMA when the
+    // volume allows 16-byte rows (else the producers gather it themselves).
+    const int n_planes = p.d_hi - p.d_lo;
+    bool vol_tma = !fused && p.vec_ok && n_planes <= 256;
 
     // Geometry for nt 8-column tiles per CTA; returns the dynamic shared
     // memory, or 0 when it does not fit (or, for two tiles, leaves fewer
@@ -1430,8 +1548,10 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
         p.rbox_bytes = static_cast<uint32_t>(8 * Cg * 128);
         p.off_l = static_cast<uint32_t>(p.n_rbox) * p.rbox_bytes;
         p.stage_slot_bytes =
-            fused ? ((p.off_l + 8u * Cg * static_cast<uint32_t>(p.l_row_bytes) + 1023) / 1024) * 1024 : 0;
-        p.stage_tx = static_cast<uint32_t>((p.n_rbox * 64 + p.l_stage_w) * 8 * Cg * 2);
+            fused ? ((p.off_l + 8u * Cg * static_cast<uint32_t>(p.l_row_bytes) + 1023) / 1024) * 1024
+                  : (vol_tma ? ((8u * 48u * static_cast<uint32_t>(n_planes) + 127) / 128) * 128 : 0);
+        p.stage_tx = fused ? static_cast<uint32_t>((p.n_rbox * 64 + p.l_stage_w) * 8 * Cg * 2)
+                           : 8u * 48u * static_cast<uint32_t>(n_planes);
         auto bar_bytes = [&](int ns) { return static_cast<uint32_t>((2 * kMaxVBuf + 1 + 2 * ns + 4) * 8 + 16); };
         auto layout = [&](int nv) -> uint32_t {  // offset of the staging ring for nv volume buffers
             uint32_t o = static_cast<uint32_t>(nsteps) * 2 * 5 * coutp * 16;
@@ -1454,10 +1574,11 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
         p.off_stage = off;
         // as many staging slots (2..kMaxSlots) as shared memory holds
         p.n_slots = 2;
-        while (fused && p.n_slots < kMaxSlots &&
+        const bool staged = fused || vol_tma;
+        while (staged && p.n_slots < kMaxSlots &&
                off + (p.n_slots + 1) * p.stage_slot_bytes <= static_cast<uint32_t>(dev.smem_optin))
             ++p.n_slots;
-        off += fused ? p.n_slots * p.stage_slot_bytes : 0;
+        off += staged ? p.n_slots * p.stage_slot_bytes : 0;
         if (off > static_cast<uint32_t>(dev.smem_optin)) return 0;
         if (nt == 2 && p.n_slots < 3) return 0;
         return off;
@@ -1471,6 +1592,10 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
         2 * n_mb * 3 * coutp <= 512)
         smem = geometry(2);
     if (smem == 0) smem = geometry(1);
+    if (vol_tma && (smem == 0 || !encode_volume_map(&p.tmap_l, vol, B, G, D_tot, H, W, 24, n_planes, 8))) {
+        vol_tma = false;  // no room for the staging ring (or no map): the producers gather
+        smem = geometry(1);
+    }
     if (smem == 0) return WW_ERR_UNSUPPORTED;
     // M-block groups: one per tile with two tiles; otherwise two from
     // kGroupMinMB M-blocks on (each group keeps at least two M-blocks
@@ -1514,7 +1639,7 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
                        : (G % 8 == 0) ? 2
                        : ((reinterpret_cast<uintptr_t>(w) % 16 == 0) && (wbytes % 16 == 0)) ? 1 : 0;
     }
-    p.use_tma = 0;
+    p.use_tma = vol_tma ? 1 : 0;
     if (fused && p.vec_ok && 8 * Cg <= 256) {
         p.use_tma = encode_feature_map(&p.tmap_l, left, B, C, in_rows, W, p.l_stage_w, 8 * Cg, false) &&
                     encode_feature_map(&p.tmap_r, right, B, C, in_rows, W, 64, 8 * Cg, true);

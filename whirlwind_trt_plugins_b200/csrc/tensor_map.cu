@@ -50,4 +50,27 @@ bool encode_feature_map(CUtensorMap* out, const void* base, int B, int C, int ro
     return r == CUDA_SUCCESS;
 }
 
+bool encode_volume_map(CUtensorMap* out, const void* base, int B, int G, int D, int H, int W, int box_x, int box_d,
+                       int box_g) noexcept
+{
+    if (out == nullptr || base == nullptr || B <= 0 || G <= 0 || D <= 0 || H <= 0 || W <= 0) return false;
+    if (W % 8 != 0 || reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+    if (box_x <= 0 || box_x > 256 || (box_x * 2) % 16 != 0) return false;
+    if (box_d <= 0 || box_d > 256 || box_g <= 0 || box_g > 256) return false;
+    const EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[5] = {static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(D),
+                                static_cast<cuuint64_t>(G), static_cast<cuuint64_t>(B)};
+    const cuuint64_t row_b = static_cast<cuuint64_t>(W) * 2;
+    const cuuint64_t plane_b = row_b * static_cast<cuuint64_t>(H);
+    const cuuint64_t strides[4] = {row_b, plane_b, plane_b * D, plane_b * D * G};
+    const cuuint32_t box[5] = {static_cast<cuuint32_t>(box_x), 1u, static_cast<cuuint32_t>(box_d),
+                               static_cast<cuuint32_t>(box_g), 1u};
+    const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+    const CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace ww

@@ -18,4 +18,10 @@ namespace ww {
 bool encode_feature_map(CUtensorMap* out, const void* base, int B, int C, int rows, int W, int box_x, int box_z,
                         bool swizzle128) noexcept;
 
+// 5-D tiled map over a contiguous [B, G, D, H, W] fp16 volume: dimensions
+// (x = W, y = row, z = disparity plane, g = group, b = batch), box
+// (box_x, 1, box_d, box_g, 1), no swizzle.  Same conditions as above.
+bool encode_volume_map(CUtensorMap* out, const void* base, int B, int G, int D, int H, int W, int box_x, int box_d,
+                       int box_g) noexcept;
+
 }  // namespace ww

@@ -315,6 +315,18 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst_saddr, const void* tmap
         : "memory");
 }
 
+// 5-D tiled TMA load global -> shared (this CTA); same rules as tma_load_3d.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst_saddr, const void* tmap, int x, int y, int z, int w, int v,
+                                            uint32_t mbar_saddr)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n"
+        :
+        : "r"(dst_saddr), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(mbar_saddr)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap)
 {
     asm volatile("prefetch.tensormap [%0];\n" : : "l"(tmap) : "memory");

@@ -36,10 +36,12 @@ Printed (rank 0, one JSON line):
 --impl reference times the CPU implementation on the same workload (rank 0
 only; the other ranks exit 0) and loads nothing from the product package.
 
-Other ops (one GPU): --op nv12_decode (camera decode), --op
-disparity_regression (soft-argmin after aggregation), --op stem3_native (the
-reference's 3-stage stem at its native shape, alone and fused with its G = 1
-correlation).
+Other ops (one GPU): --op corr_volume (the standalone group-wise CorrVolume,
+HBM roofline, end to end from pinned host buffers), --op cost_stem3d (the
+generalised stem on a configuration's volume, tensor roofline), --op
+nv12_decode (camera decode), --op disparity_regression (soft-argmin after
+aggregation), --op stem3_native (the reference's 3-stage stem at its native
+shape, alone and fused with its G = 1 correlation).
 """
 from __future__ import annotations
 
@@ -97,12 +99,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=None,
-                    help=f"configuration (default {DEFAULT_CONFIG}; --op corr_volume: {CORR_VOLUME_CONFIG})")
+                    help=f"configuration (default {DEFAULT_CONFIG}; --op corr_volume / cost_stem3d: "
+                         f"{CORR_VOLUME_CONFIG})")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the configuration's batch (profiling captures of a smaller case)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["corr_cost_stem3d", "corr_volume", "nv12_decode", "disparity_regression",
-                                     "stem3_native"],
+    ap.add_argument("--op", choices=["corr_cost_stem3d", "corr_volume", "cost_stem3d", "nv12_decode",
+                                     "disparity_regression", "stem3_native"],
                     default="corr_cost_stem3d")
     ap.add_argument("--corr-engine", choices=["tensor", "cuda_cores"], default="tensor",
                     help="correlation engine of the fused op (ww_set_fused_corr_engine)")
@@ -961,6 +964,84 @@ def bench_disparity(args):
     print(json.dumps(line), flush=True)
 
 
+def bench_stem_volume(args):
+    """The generalised CostStem3D (volume form, ww_cost_stem3d) on a
+    configuration's group-wise volume (--config, default 2; --batch to scale):
+    one step = one launch over a [B, G, D, H, W] fp16 volume made by
+    ww_corr_volume from the configuration's features.  value: voxels/s
+    (B*D*H*W); roofline against the tensor peak with the stem's FLOPs."""
+    import torch
+    import whirlwind_trt_plugins_b200 as ww
+    C_ = load_configs()
+    cfg = C_.CONFIGS[args.config or CORR_VOLUME_CONFIG]
+    if args.batch:
+        cfg = cfg.scaled(B=args.batch)
+    torch.cuda.set_device(0)
+    B, G, D, H, W, Cout = cfg.B, cfg.G, cfg.D, cfg.H, cfg.W, cfg.Cout
+    vol_bytes, out_bytes = B * G * D * H * W * 2, B * Cout * D * H * W * 2
+    n_sets = max(2, -(-400 * 2**20 // (vol_bytes + out_bytes)))  # > 126 MB of L2
+    sets = []
+    for k in range(n_sets):
+        x = C_.make_inputs_torch(cfg, torch.device("cuda", 0), seed=21 + k)
+        vol = ww.corr_volume(x["left"], x["right"], D, G)
+        del x["left"], x["right"]
+        sets.append((vol, x["w"], x["b"], torch.empty((B, Cout, D, H, W), dtype=torch.float16, device="cuda")))
+    stream = torch.cuda.current_stream()
+
+    def step(i, st):
+        v, w, b, o = sets[i % n_sets]
+        ww.cost_stem3d(v, w, b, act=cfg.act, out=o, stream=st)
+
+    for i in range(max(3, args.warmup)):
+        step(i, stream)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            step(i, stream)
+        torch.cuda.synchronize()
+        print(f"profile run: cost_stem3d {cfg.name}, {max(3, args.warmup)} + {args.steps} launches", flush=True)
+        return
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(args.steps):
+            step(i, torch.cuda.current_stream())
+    stream.wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        t_end = time.time() + 1.0  # the sampler needs load for a few of its 200 ms periods
+        while time.time() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    del graph
+    voxels = B * D * H * W
+    flops = 2.0 * B * Cout * G * 27 * D * H * W
+    peaks = load_peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "cost voxels/s (B*D*H*W) 3D stem, volume form", "value": voxels / (ms * 1e-3),
+        "unit": "voxels/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (the configuration's features through ww_corr_volume)",
+        "config": {"workload": f"cost_stem3d {workload_name(cfg)}",
+                   "l2": f"{n_sets} rotating volume/output sets > 126 MB L2",
+                   "timing": "the K launches replayed from one CUDA graph"},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["tflops"], "unit": "TFLOP/s",
+                     "frac": tf / peaks["tflops"], "traffic": None, "peak_source": peaks["src"],
+                     "hbm_gbs": (vol_bytes + out_bytes) / (ms * 1e-3) / 1e9},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def bench_stem3_native(args):
     """The reference's 3-stage CostStem3D at its native shape [1, 1, 48, 32,
     40] (1 -> 4 -> 4 -> 1, ReLU6), alone (ww_cost_stem3d_ref3) and fused with
@@ -1025,7 +1106,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.op != "corr_cost_stem3d":
         if rank == 0 and args.impl == "ours":
-            {"corr_volume": bench_corr_volume, "nv12_decode": bench_nv12, "disparity_regression": bench_disparity,
+            {"corr_volume": bench_corr_volume, "cost_stem3d": bench_stem_volume, "nv12_decode": bench_nv12, "disparity_regression": bench_disparity,
              "stem3_native": bench_stem3_native}[args.op](args)
         return
     if args.config is None:

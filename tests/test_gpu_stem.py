@@ -111,13 +111,15 @@ def test_stem_tc_matches_oracle(ww, torch, orc, case, act):
     dict(B=2, Cin=40, Cout=32, D=48, H=6, W=40),
     dict(B=1, Cin=12, Cout=16, D=64, H=5, W=32),     # a partial octet
     dict(B=1, Cin=8, Cout=16, D=200, H=3, W=16),     # disparity bands
+    dict(B=1, Cin=24, Cout=16, D=200, H=3, W=16),    # 160-plane band: no room for the staging ring
 ])
 def test_stem_volume_gather_paths_agree(ww, torch, case):
-    """The volume form's two gathers -- 16-byte loads with a register
-    transpose (W % 8 == 0, 16-byte aligned volume) and 2-byte loads (any
-    other volume) -- fill the same volume rows, so the outputs are equal bit
-    for bit; the 2-byte path is reached by passing a volume that starts one
-    element into its storage."""
+    """The volume form's gathers -- TMA-staged boxes or, where shared memory
+    has no room for the staging ring (the 160-plane band of the last case),
+    16-byte loads, both with a register transpose (W % 8 == 0, 16-byte
+    aligned volume), and 2-byte loads (any other volume) -- fill the same
+    volume rows, so the outputs are equal bit for bit; the 2-byte path is
+    reached by passing a volume that starts one element into its storage."""
     B, Cin, Cout, D, H, W = (case[k] for k in ("B", "Cin", "Cout", "D", "H", "W"))
     g = torch.Generator().manual_seed(Cin + D)
     n = B * Cin * D * H * W

@@ -336,22 +336,34 @@ def make_sets(C, cfg, ctx, b_local: int, n_max: int):
     return sets
 
 
-def time_steps(ctx, step, steps: int, soak_s: float, clocks: bool):
+def soak(step, soak_s: float, soak_steps: int | None, sync) -> int:
+    """Untimed steps before a timed region: for soak_s seconds of wall time,
+    or exactly soak_steps steps when given; `sync` every 16 steps.  Returns
+    the number of steps run."""
+    t_end = time.time() + soak_s
+    i = 0
+    while (i < soak_steps) if soak_steps is not None else (time.time() < t_end):
+        step(i)
+        i += 1
+        if i % 16 == 0:
+            sync()
+    return i
+
+
+def time_steps(ctx, step, steps: int, soak_s: float, clocks: bool, soak_steps: int | None = None):
     """CUDA-event time (ms) of exactly `steps` steps after a soak, max over
-    ranks; nvidia-smi clocks sampled during the soak and the timed region."""
+    ranks; nvidia-smi clocks sampled during the soak and the timed region.
+    The soak runs for soak_s seconds of wall time -- a different number of
+    steps on each rank, so only for steps without a collective -- or, given
+    soak_steps, exactly that many steps on every rank (steps that exchange
+    data between ranks must all take the same collective calls)."""
     import torch
     stream = torch.cuda.current_stream()
     sampler = ClockSampler(ctx.local) if clocks else None
     if sampler is not None:
         sampler.__enter__()
     try:
-        t_end = time.time() + soak_s
-        i = 0
-        while time.time() < t_end:
-            step(i)
-            i += 1
-            if i % 16 == 0:
-                torch.cuda.synchronize()
+        soak(step, soak_s, soak_steps, torch.cuda.synchronize)
         torch.cuda.synchronize()
         ctx.barrier()
         torch.cuda.synchronize()
@@ -548,7 +560,9 @@ def bench_rows(args, C, ww, cfg, ctx, steps: int) -> dict:
     for i in range(max(3, args.warmup)):
         step(i)
     torch.cuda.synchronize()
-    ms, _ = time_steps(ctx, step, steps, 0.3, False)
+    # The step exchanges halo rows (NCCL send/recv): a fixed soak count, the
+    # same on every rank.
+    ms, _ = time_steps(ctx, step, steps, 0.0, False, soak_steps=100)
     return {"config": config_dict(cfg, ctx.world, "rows"), "value": cfg.voxels * steps / (ms * 1e-3),
             "unit": UNIT, "ms_per_step": ms / steps, "scaling": "strong",
             "gpu_launches": steps, "halo_bytes_per_rank_step": 2 * 2 * cfg.B * cfg.C * cfg.W * 2}

@@ -218,3 +218,36 @@ def test_haloband_holds_rows_and_halo(tmp_path, world):
         assert (i0, i1) == halo_rows(SHAPE["H"], r0, r1)
         band = np.load(tmp_path / f"hb{r}.npy")
         assert np.array_equal(band.view(np.uint16), L[:, :, i0:i1].view(np.uint16))
+
+
+def _soak_worker(rank, world, port, outdir):
+    """Steps that each take a collective (as the row-band bench's halo
+    exchange does), with per-rank step times that differ: a soak by step count
+    keeps every rank on the same collective calls."""
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    import torch
+    import bench
+    dist = _init(rank, world, port, timeout_s=15)
+    try:
+        t = torch.zeros(1)
+
+        def step(i):
+            time.sleep(0.002 * (rank + 1))  # rank-dependent step time
+            t.fill_(i)
+            dist.all_reduce(t)
+
+        n = bench.soak(step, 0.0, 12, lambda: None)
+        dist.barrier()
+        np.save(os.path.join(outdir, f"soak{rank}.npy"), np.array([n, float(t.item())]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_soak_by_count_keeps_ranks_in_step(tmp_path):
+    codes = _run(3, _soak_worker, (str(tmp_path),), timeout=60)
+    assert codes == [0, 0, 0]
+    got = [np.load(tmp_path / f"soak{r}.npy") for r in range(3)]
+    assert all(g[0] == 12 for g in got)
+    assert all(g[1] == 3 * 11 for g in got)  # the last step's all-reduce of i = 11 over 3 ranks

@@ -375,6 +375,62 @@ __device__ __forceinline__ uint32_t scale2_to_half2(float x, float y, float s)
     return *reinterpret_cast<const uint32_t*>(&h2);
 }
 
+// The general epilogue of one disparity's VW columns (gx .. gx + VW - 1) of a
+// row-streaming register tile under scale rule RULE, as packed fp16 pairs:
+// acc / Cg (kRuleDivide: the correction step of int_div.cuh for every value)
+// or acc * (1 / Cg), and, under kRuleZero, an explicit +0 where w - d < 0.
+// Returns whether some value was outside the correction step's exact range;
+// the caller then rewrites its tile with corr_rows_exact, so the common path
+// has no per-value branch.
+template <int VW, int RULE>
+__device__ __forceinline__ bool scale_cols(const float (&acc)[VW], int gx, int d, int Cg, float inv_cg,
+                                           uint32_t (&h)[VW / 2])
+{
+    bool redo = false;
+#pragma unroll
+    for (int v = 0; v < VW; v += 2) {
+        float q[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float a = acc[v + k];
+            if constexpr ((RULE & kRuleDivide) != 0) {
+                q[k] = div_by_int_core(a, static_cast<float>(Cg), inv_cg);
+                redo |= !div_by_int_in_range(a);
+            } else {
+                q[k] = __fmul_rn(a, inv_cg);
+            }
+            if ((RULE & kRuleZero) != 0 && gx + v + k < d) q[k] = 0.0f;  // naive rule: w - d < 0 is +0
+        }
+        const __half2 h2 = __floats2half2_rn(q[0], q[1]);
+        h[v / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    return redo;
+}
+
+// The rare path of the divide rule: a thread whose tile held a value outside
+// the correction step's range recomputes its ND x VW outputs from the staged
+// row (the same fp32 fma chain in channel order from +0, so the same sums),
+// divides with div_int and stores them one by one over what it stored.
+// Not inlined: the common path keeps the registers the division subroutine
+// would need.
+template <int VW>
+__device__ __noinline__ void corr_rows_exact(const __half* Ls, const __half* Rs, int tw, int RW, int wl, int rs,
+                                             int Cg, float inv_cg, int dd0, int D, int gx, int W, bool zero_rule,
+                                             __half* op, int64_t plane)
+{
+    constexpr int ND = kDispPerThread;
+    const unsigned short* L = reinterpret_cast<const unsigned short*>(Ls);
+    const unsigned short* R = reinterpret_cast<const unsigned short*>(Rs);
+    for (int dd = 0; dd < ND && dd0 + dd < D; ++dd)
+        for (int v = 0; v < VW && gx + v < W; ++v) {
+            float a = 0.0f;
+            for (int c = 0; c < Cg; ++c) a = fma_h(L[c * tw + wl + v], R[c * RW + rs + ND - dd + v], a);
+            float q = div_int(a, Cg, inv_cg);
+            if (zero_rule && gx + v < dd0 + dd) q = 0.0f;
+            op[dd * plane + v] = __float2half_rn(q);
+        }
+}
+
 // fp16, W > 64, W % 8 == 0, the group's channels in one staged chunk
 // (Cg <= CC) and all disparities in one band.  The register tile and the
 // arithmetic are corr_volume_h_kernel's (4 columns x 8 disparities per
@@ -397,13 +453,15 @@ __device__ __forceinline__ uint32_t scale2_to_half2(float x, float y, float s)
 // from one thread, and selecting the w - d < 0 zeros before a shared
 // packed epilogue.
 // CG: channels per group when known at compile time (the channel loop is
-// then unrolled with immediate offsets), 0 otherwise.  64 registers: 4 CTAs
-// of 240 threads per SM (measured faster than 80 registers and 3 CTAs on
-// every benchmark shape but config 2, where it is 4 % slower).
-template <int CC, int CG>
+// then unrolled with immediate offsets), 0 otherwise.  RULE: the scale rule
+// (kRuleDivide | kRuleZero bits), a compile-time constant so the epilogue
+// carries no per-value rule tests.  64 registers: 4 CTAs of 240 threads per
+// SM (measured faster than 80 registers and 3 CTAs on every benchmark shape
+// but config 2, where it is 4 % slower).
+template <int CC, int CG, int RULE>
 __global__ void __maxnreg__(64) corr_volume_rows_kernel(
     const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
-    int C, int H, int W, int D, int G, int rows, int tw, int rule, float inv_cg)
+    int C, int H, int W, int D, int G, int rows, int tw, float inv_cg)
 {
     constexpr int ND = kDispPerThread;
     const int DT = ND * blockDim.y;
@@ -433,10 +491,10 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
     // from right columns staged as zeros: +0 for finite features, exactly
     // what the zero-filled staging gives here, so those outputs need no test.
     // Under the naive rule (:75-86) they are an explicit +0.
-    // rule: kRuleDivide (acc / Cg; otherwise * (1 / Cg), the same when Cg
+    // RULE: kRuleDivide (acc / Cg; otherwise * (1 / Cg), the same when Cg
     // is a power of two) | kRuleZero (the naive rule's explicit +0).
-    const bool divide = (rule & kRuleDivide) != 0;
-    const bool zero_rule = (rule & kRuleZero) != 0;
+    constexpr bool divide = (RULE & kRuleDivide) != 0;
+    constexpr bool zero_rule = (RULE & kRuleZero) != 0;
     const bool plain = dd0 + ND <= D && gx + kVecW <= W && !divide && !(zero_rule && gx < dd0 + ND - 1);
     __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
 
@@ -490,27 +548,25 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
                 *reinterpret_cast<uint2*>(op + dd * plane) = u;
             }
         } else if (gx < W) {
+            bool redo = false;
 #pragma unroll
             for (int dd = 0; dd < ND; ++dd) {
                 const int d = dd0 + dd;
                 if (d >= D) break;
-                __half tmp[kVecW];
-#pragma unroll
-                for (int v = 0; v < kVecW; ++v) {
-                    float val;
-                    if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
-                    else val = divide ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
-                    tmp[v] = __float2half_rn(val);
-                }
+                uint32_t hv[kVecW / 2];
+                redo |= scale_cols<kVecW, RULE>(acc[dd], gx, d, Cg, inv_cg, hv);
                 __half* o = op + dd * plane;
                 if (gx + kVecW <= W) {
-                    *reinterpret_cast<uint2*>(o) = *reinterpret_cast<uint2*>(tmp);
+                    *reinterpret_cast<uint2*>(o) = make_uint2(hv[0], hv[1]);
                 } else {
 #pragma unroll
                     for (int v = 0; v < kVecW; ++v)
-                        if (gx + v < W) o[v] = tmp[v];
+                        if (gx + v < W)
+                            o[v] = __ushort_as_half(static_cast<unsigned short>(hv[v / 2] >> (16 * (v & 1))));
                 }
             }
+            if (divide && redo)
+                corr_rows_exact<kVecW>(Ls, Rs, tw, RW, wl, rs, Cg, inv_cg, dd0, D, gx, W, zero_rule, op, plane);
         }
     }
 }
@@ -521,10 +577,10 @@ __global__ void __maxnreg__(64) corr_volume_rows_kernel(
 // bytes per disparity, so loads, epilogue and per-row overhead per output
 // are about half.  Same arithmetic, so bit-identical results.  blockDim =
 // (tw / 8, ny), DT = 8 ny.
-template <int CC, int CG>
+template <int CC, int CG, int RULE>
 __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
     const __half* __restrict__ left, const __half* __restrict__ right, __half* __restrict__ out,
-    int C, int H, int W, int D, int G, int rows, int tw, int rule, float inv_cg)
+    int C, int H, int W, int D, int G, int rows, int tw, float inv_cg)
 {
     constexpr int ND = kDispPerThread;
     constexpr int VW = 8;
@@ -549,8 +605,8 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
     const int rs = wl - dd0 - ND + DT;  // 8-aligned: right value k (0..15) is column wl - dd0 - 8 + k
     const int gx = w0 + wl;
     const bool full_cols = gx + VW <= W;
-    const bool divide = (rule & kRuleDivide) != 0;  // as in corr_volume_rows_kernel
-    const bool zero_rule = (rule & kRuleZero) != 0;
+    constexpr bool divide = (RULE & kRuleDivide) != 0;  // as in corr_volume_rows_kernel
+    constexpr bool zero_rule = (RULE & kRuleZero) != 0;
     const bool plain = dd0 + ND <= D && full_cols && !divide && !(zero_rule && gx < dd0 + ND - 1);
     __half* obase = out + ((i64(b) * G + g) * D + dd0) * plane + gx;
 
@@ -609,27 +665,25 @@ __global__ void __maxnreg__(128) corr_volume_rows8_kernel(
                 *reinterpret_cast<uint4*>(op + dd * plane) = u;
             }
         } else if (gx < W) {
+            bool redo = false;  // as in corr_volume_rows_kernel
 #pragma unroll
             for (int dd = 0; dd < ND; ++dd) {
                 const int d = dd0 + dd;
                 if (d >= D) break;
-                __half tmp[VW];
-#pragma unroll
-                for (int v = 0; v < VW; ++v) {
-                    float val;
-                    if (zero_rule && gx + v < d) val = 0.0f;  // naive rule: w - d < 0 is an explicit +0
-                    else val = divide ? div_int(acc[dd][v], Cg, inv_cg) : __fmul_rn(acc[dd][v], inv_cg);
-                    tmp[v] = __float2half_rn(val);
-                }
+                uint32_t hv[VW / 2];
+                redo |= scale_cols<VW, RULE>(acc[dd], gx, d, Cg, inv_cg, hv);
                 __half* o = op + dd * plane;
                 if (full_cols) {
-                    *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(tmp);
+                    *reinterpret_cast<uint4*>(o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 } else {
 #pragma unroll
                     for (int v = 0; v < VW; ++v)
-                        if (gx + v < W) o[v] = tmp[v];
+                        if (gx + v < W)
+                            o[v] = __ushort_as_half(static_cast<unsigned short>(hv[v / 2] >> (16 * (v & 1))));
                 }
             }
+            if (divide && redo)
+                corr_rows_exact<VW>(Ls, Rs, tw, RW, wl, rs, Cg, inv_cg, dd0, D, gx, W, zero_rule, op, plane);
         }
     }
 }
@@ -715,6 +769,34 @@ int int_div_selftest(int b, unsigned long long* mismatches) noexcept
     if (cudaMemcpyFromSymbol(mismatches, g_int_div_mismatch, sizeof(*mismatches)) != cudaSuccess)
         return launch_status("ww_selftest_int_division");
     return WW_SUCCESS;
+}
+
+// The row-streaming kernel for a group width and scale rule (the width
+// unrolled when it is 4, 8, 12 or 16; the rule always a template constant);
+// eight: the 8 x 8 register tile, else the 4 x 8 one.
+using RowsFn = void (*)(const __half*, const __half*, __half*, int, int, int, int, int, int, int, float);
+
+template <int RULE>
+RowsFn rows_kernel_for(int Cg, bool eight)
+{
+    if (eight)
+        return Cg == 4    ? corr_volume_rows8_kernel<kChunkC, 4, RULE>
+               : Cg == 8  ? corr_volume_rows8_kernel<kChunkC, 8, RULE>
+               : Cg == 12 ? corr_volume_rows8_kernel<kChunkC, 12, RULE>
+               : Cg == 16 ? corr_volume_rows8_kernel<kChunkC, 16, RULE>
+                          : corr_volume_rows8_kernel<kChunkC, 0, RULE>;
+    return Cg == 4    ? corr_volume_rows_kernel<kChunkC, 4, RULE>
+           : Cg == 8  ? corr_volume_rows_kernel<kChunkC, 8, RULE>
+           : Cg == 12 ? corr_volume_rows_kernel<kChunkC, 12, RULE>
+           : Cg == 16 ? corr_volume_rows_kernel<kChunkC, 16, RULE>
+                      : corr_volume_rows_kernel<kChunkC, 0, RULE>;
+}
+
+RowsFn rows_kernel(int Cg, int rule, bool eight)
+{
+    if (rule == 0) return rows_kernel_for<0>(Cg, eight);
+    if (rule == kRuleZero) return rows_kernel_for<kRuleZero>(Cg, eight);
+    return rows_kernel_for<kRuleZero | kRuleDivide>(Cg, eight);
 }
 
 // Scale rule of the reference kernel that launchCorrVolume<T> would run for a
@@ -820,13 +902,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
         const int ny8 = max(1, min((D + kDispPerThread - 1) / kDispPerThread, 512 / tx8));
         const int DT8 = ny8 * kDispPerThread;
         if (vec_ok && DT8 >= D && D <= 48 && Cg >= 8 && Cg <= cc) {
-            using RowsFn = void (*)(const __half*, const __half*, __half*, int, int, int, int, int, int, int, int,
-                                    float);
-            RowsFn kern = Cg == 4    ? corr_volume_rows8_kernel<kChunkC, 4>
-                          : Cg == 8  ? corr_volume_rows8_kernel<kChunkC, 8>
-                          : Cg == 12 ? corr_volume_rows8_kernel<kChunkC, 12>
-                          : Cg == 16 ? corr_volume_rows8_kernel<kChunkC, 16>
-                                     : corr_volume_rows8_kernel<kChunkC, 0>;
+            const RowsFn kern = rows_kernel(Cg, rule, true);
             const size_t rsmem = 3 * static_cast<size_t>(cc) * (2 * tw + DT8) * 2;
             int resident = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, tx8 * ny8, rsmem) != cudaSuccess ||
@@ -844,8 +920,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             dim3 block(tx8, ny8);
             dim3 grid(nt, (H + best - 1) / best, B * G);
             kern<<<grid, block, rsmem, stream>>>(static_cast<const __half*>(left), static_cast<const __half*>(right),
-                                                 static_cast<__half*>(out), C, H, W, D, G, best, tw, rule,
-                                                 inv_cg);
+                                                 static_cast<__half*>(out), C, H, W, D, G, best, tw, inv_cg);
             return launch_status("ww_corr_volume");
         }
         if (vec_ok && n_dband == 1 && Cg <= cc) {
@@ -853,13 +928,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             // per CTA chosen to minimise (waves of resident CTAs) x (rows
             // per CTA + 1 for the first row's copy).
             const size_t rsmem = 3 * smem;  // three staged rows
-            using RowsFn = void (*)(const __half*, const __half*, __half*, int, int, int, int, int, int, int, int,
-                                    float);
-            RowsFn kern = Cg == 4    ? corr_volume_rows_kernel<kChunkC, 4>
-                          : Cg == 8  ? corr_volume_rows_kernel<kChunkC, 8>
-                          : Cg == 12 ? corr_volume_rows_kernel<kChunkC, 12>
-                          : Cg == 16 ? corr_volume_rows_kernel<kChunkC, 16>
-                                     : corr_volume_rows_kernel<kChunkC, 0>;
+            const RowsFn kern = rows_kernel(Cg, rule, false);
             int resident = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, tx * ny, rsmem) != cudaSuccess ||
                 resident < 1)
@@ -877,7 +946,7 @@ int corr_volume_launch(const void* left, const void* right, void* out, int dtype
             dim3 grid(nt, (H + best - 1) / best, B * G);
             kern<<<grid, block, rsmem, stream>>>(
                 static_cast<const __half*>(left), static_cast<const __half*>(right), static_cast<__half*>(out), C,
-                H, W, D, G, best, tw, rule, inv_cg);
+                H, W, D, G, best, tw, inv_cg);
             return launch_status("ww_corr_volume");
         }
         dim3 block(tx, ny);

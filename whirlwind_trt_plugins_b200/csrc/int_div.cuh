@@ -13,8 +13,10 @@
 //     r  = a - b q              (exact with one fma while q is within an ulp)
 //     q' = RN(q + r y)          = RN(a / b)
 //
-// Inputs whose quotient may leave the normal range (|a| < 2^-100), and
-// infinities and NaNs, take the rounded division itself.  The library uses
+// Nonzero inputs whose quotient may leave the normal range (|a| < 2^-100),
+// and infinities and NaNs, take the rounded division itself; tiled kernels
+// evaluate the step for a whole register tile, note whether any input was out
+// of range, and redo only such a tile with div_int.  The library uses
 // this only for divisors 3..kMaxIntDivisor that are not powers of two (for
 // those a multiply by 1/b is exact), and `ww_selftest_int_division` compares
 // it with the rounded division on all 2^32 fp32 inputs for each such divisor
@@ -27,13 +29,27 @@ namespace ww {
 
 constexpr int kMaxIntDivisor = 1024;
 
-__device__ __forceinline__ float div_by_int(float a, float b, float y)
+// Whether div_by_int_core is exact for a: a = +-0 or 2^-100 <= |a| <= the
+// largest finite float.
+__device__ __forceinline__ bool div_by_int_in_range(float a)
 {
     const float m = fabsf(a);
-    if (!(m >= 0x1p-100f && m <= 0x1.fffffep127f)) return __fdiv_rn(a, b);
+    return m == 0.0f || (m >= 0x1p-100f && m <= 0x1.fffffep127f);
+}
+
+// The correction step without the range check.  For a = +-0 the step
+// yields +0 (r = +0, and +0 + -0 is +0), so the sign of a is put back: every
+// quotient here has the sign of a (b > 0).
+__device__ __forceinline__ float div_by_int_core(float a, float b, float y)
+{
     const float q = __fmul_rn(a, y);
     const float r = __fmaf_rn(-q, b, a);
-    return __fmaf_rn(r, y, q);
+    return copysignf(__fmaf_rn(r, y, q), a);
+}
+
+__device__ __forceinline__ float div_by_int(float a, float b, float y)
+{
+    return div_by_int_in_range(a) ? div_by_int_core(a, b, y) : __fdiv_rn(a, b);
 }
 
 // a / b rounded to nearest for an integer divisor b >= 1 with y = RN(1 / b):

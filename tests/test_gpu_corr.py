@@ -135,6 +135,32 @@ def test_corr_edge_cases(ww, torch, orc, case, dtype):
         assert not np.any(_bits(o[:, :, d, :, :d]))
 
 
+@pytest.mark.parametrize("D", [40, 56])  # the 8 x 8 and the 4 x 8 row-streaming tiles
+@pytest.mark.parametrize("G", [2, 6])    # Cg = 12 (divided) and 4 (multiplied), both under the naive rule
+def test_corr_nonfinite_and_extreme_features(ww, torch, orc, D, G):
+    """Infinite, NaN, signed-zero and near-overflow features under the naive
+    scale rule: the row kernels' division takes its exact path for tiles
+    holding a non-finite sum, and every finite output stays bit-identical to
+    the oracle (NaN outputs compared as NaN, whatever their payload)."""
+    rng = np.random.default_rng(D + G)
+    L = rng.standard_normal((1, 24, 4, 96)).astype(np.float16)
+    R = rng.standard_normal((1, 24, 4, 96)).astype(np.float16)
+    L[0, 3, 1, 10] = np.inf
+    R[0, 5, 2, 50] = -np.inf
+    L[0, 14, 0, 70] = np.nan
+    L[0, 7, 3, 20:28] = 60000.0
+    R[0, 7, 3, 0:40] = -60000.0
+    L[0, 9, :, 30:40] = -0.0
+    R[0, 9, :, :] = 0.0
+    out = _run(ww, torch, L, R, D, G)
+    ref = orc.corr_f16(L, R, D, G)
+    nan_o, nan_r = np.isnan(out), np.isnan(ref)
+    assert np.array_equal(nan_o, nan_r)
+    assert np.isinf(out).any() and nan_o.any()
+    assert np.array_equal(_bits(np.where(nan_o, 0, out).astype(np.float16)),
+                          _bits(np.where(nan_r, 0, ref).astype(np.float16)))
+
+
 def test_corr_unaligned_pointers(ww, torch, orc):
     rng = np.random.default_rng(99)
     L = rng.standard_normal((1, 16, 4, 64)).astype(np.float16)

@@ -279,17 +279,13 @@ __device__ __forceinline__ int tile_row_wp(int row)
     return row < 8 ? row + 1 : (row == 8 ? 0 : (row == 9 ? 9 : kWtp));
 }
 
-// (x * s, y * s) with one packed fp32 multiply (each lane rounded as
-// __fmul_rn), converted to a half2 (x in the low half).
-__device__ __forceinline__ uint32_t scale_to_half2(float x, float y, float s)
+// (x * s, y * s) (each rounded as __fmul_rn) converted to a half2 (x in the
+// low half).  Two scalar multiplies: a packed f32x2 multiply of values from
+// two accumulator arrays needed register moves to pair them, which made the
+// correlation's tile store ~8 % of config 4's time (measured).
+__device__ __forceinline__ uint32_t scale_pair(float x, float y, float s)
 {
-    uint64_t v, sv, r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(x), "f"(y));
-    asm("mov.b64 %0, {%1, %1};" : "=l"(sv) : "f"(s));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(v), "l"(sv));
-    float a, b;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-    const __half2 h2 = __floats2half2_rn(a, b);
+    const __half2 h2 = __floats2half2_rn(__fmul_rn(x, s), __fmul_rn(y, s));
     return *reinterpret_cast<const uint32_t*>(&h2);
 }
 
@@ -299,29 +295,32 @@ __device__ __forceinline__ uint32_t scale_to_half2(float x, float y, float s)
 // w' = tile_row_wp(row)), column 2q + (s & 1) of right tile jt (staged right
 // index 8 jt + 2q + (s & 1)), i.e. disparity d = 8 ceil(D/8) - 1 + w' - index.
 //
-// Lanes with q >= 2 visit the two slots of a pair in the opposite order:
-// then the 8 lanes of each quarter warp write 8 distinct 16-byte bank groups
-// in every store (in slot order, lanes q and q + 2 would collide).
+// In slot order lanes q and q + 2 of a quarter warp write the same 16-byte
+// bank group (their disparities differ by 4 planes of 160 bytes), a two-way
+// conflict per store; letting the lanes with q >= 2 visit a pair's slots in
+// the opposite order avoided it but cost a select per stored word, which
+// measured slower (config 4 at B = 16 2053 against 1997 us).
 __device__ __forceinline__ void store_corr_tile(const StemParams& p, const float (&acc)[8][4], uint32_t vsa,
                                                 int jt, int lane)
 {
     const int m = lane >> 2, q = lane & 3;
-    const bool flip = (q & 2) != 0;
     const int dbase = 8 * (p.n_tiles - 2) - 1;
     const float inv_cg = p.inv_cg;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int wp = tile_row_wp(m + 8 * (i >> 1));
-        const int d = dbase + wp - (8 * jt + 2 * q + ((i & 1) ^ (flip ? 1 : 0)));
-        if (wp < kWtp && d >= p.d_lo && d < p.d_hi) {
-            uint32_t h[4];
+    for (int pr = 0; pr < 2; ++pr) {  // slots 2 pr, 2 pr + 1: one volume column, two right columns
+        const int wp = tile_row_wp(m + 8 * pr);
+        uint32_t h[2][4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float a0 = flip ? acc[2 * k][i ^ 1] : acc[2 * k][i];
-                const float a1 = flip ? acc[2 * k + 1][i ^ 1] : acc[2 * k + 1][i];
-                h[k] = scale_to_half2(a0, a1, inv_cg);
-            }
-            st_shared_v4(vsa + static_cast<uint32_t>(((d + 1) * kWtp + wp) * 16), h[0], h[1], h[2], h[3]);
+        for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                h[s2][k] = scale_pair(acc[2 * k][2 * pr + s2], acc[2 * k + 1][2 * pr + s2], inv_cg);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int d = dbase + wp - (8 * jt + 2 * q + t);
+            if (wp < kWtp && d >= p.d_lo && d < p.d_hi)
+                st_shared_v4(vsa + static_cast<uint32_t>(((d + 1) * kWtp + wp) * 16), h[t][0], h[t][1], h[t][2],
+                             h[t][3]);
         }
     }
 }
@@ -622,8 +621,8 @@ __device__ __forceinline__ void corr_item_fma(const StemParams& p, const uint8_t
                 v.x = *reinterpret_cast<const uint32_t*>(&h01);
                 v.y = *reinterpret_cast<const uint32_t*>(&h23);
             } else {
-                v.x = scale_to_half2(acc[0][j], acc[1][j], p.inv_cg);
-                v.y = scale_to_half2(acc[2][j], acc[3][j], p.inv_cg);
+                v.x = scale_pair(acc[0][j], acc[1][j], p.inv_cg);
+                v.y = scale_pair(acc[2][j], acc[3][j], p.inv_cg);
             }
             *reinterpret_cast<uint2*>(row0 - j * kWtp * 16) = v;
         }

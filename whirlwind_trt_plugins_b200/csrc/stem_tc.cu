@@ -101,6 +101,7 @@ constexpr int kLRowBytes = kLStageW * 2;
 constexpr int kMaxSteps = 32;      // K-steps per M-block (group octets <= 7)
 constexpr int kMaxSlots = 8;       // staging ring depth
 constexpr int kMaxVBuf = 3;        // volume row buffers
+constexpr int kMaxTasks = 24;      // producer tasks per staging job (two right tiles each)
 constexpr int kGroupMinMB = 4;     // M-blocks from which a row is issued and drained as two groups
 constexpr bool kDualTiles = true;  // two 8-column tiles per CTA where tensor memory holds them
 constexpr int kMaxFItems = 10 * 24;  // CUDA-core correlation items per job (10 columns x ceil(D/8) + 2 tiles)
@@ -133,6 +134,7 @@ struct StemParams {
     int n_vbuf;               // volume row buffers (2..kMaxVBuf)
     int n_tiles;              // 8-column right tiles per job: ceil(D/8) + 2
     int tpj;                  // producer tasks per job (each a range of right tiles)
+    uint8_t task_jt[kMaxTasks + 1];  // task hh covers right tiles [task_jt[hh], task_jt[hh + 1])
     int raw_w_smem;           // weights staged through shared memory at set-up: 2 transposed, 1 as is, 0 not
     int use_tma;              // 1: jobs staged by TMA (else cp.async / scalar copies)
     int out_vec;              // 1: W % 8 == 0 and 16-byte aligned output (16-byte row stores)
@@ -765,21 +767,23 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     // image and past the last channel).  Volume mode: one box of the volume,
     // [8 groups][planes d_lo .. d_hi - 1][columns w0 - 8 .. w0 + 15] (zero
     // fill outside the image and past the last group).
+    // The ring position (slot, row offset jr = j / KG, octet kg = j % KG) is
+    // passed in: the loops keep it as running counters, without a division
+    // per job.
     const int n_runs = p.n8;
-    auto tma_job = [&](int j) {
-        const int slot = j % p.n_slots;
+    auto tma_job = [&](int slot, int jr, int kg) {
         const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
         const uint32_t full = smem_addr(&stage_full[slot]);
         mbar_arrive_expect_tx(full, p.stage_tx);
         if constexpr (FUSED) {
-            const int urow = uv0 + j / p.KG - p.in_row0;
-            const int c0 = (j % p.KG) * 8 * p.Cg;
+            const int urow = uv0 + jr - p.in_row0;
+            const int c0 = kg * 8 * p.Cg;
             for (int k = 0; k < p.n_rbox; ++k)
                 tma_load_4d(sbase + k * p.rbox_bytes, &p.tmap_r, w0 - 8 * n_runs - p.d_off + 64 * k, urow, c0, b,
                             full);
             tma_load_4d(sbase + p.off_l, &p.tmap_l, w0 - 8, urow, c0, b, full);
         } else {
-            tma_load_5d(sbase, &p.tmap_l, w0 - 8, uv0 + j / p.KG, p.d_off + p.d_lo, 8 * (j % p.KG), b, full);
+            tma_load_5d(sbase, &p.tmap_l, w0 - 8, uv0 + jr, p.d_off + p.d_lo, 8 * kg, b, full);
         }
     };
     // The first n_slots jobs need no free slot: issue them now, so their
@@ -788,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
     const int n_pre = (p.use_tma && wmode != 0) ? min(p.n_slots, total_jobs) : 0;
     if (n_pre > 0 && warp == kLoadWarp) {
         if (elect_one())
-            for (int j = 0; j < n_pre; ++j) tma_job(j);
+            for (int j = 0; j < n_pre; ++j) tma_job(j, j / p.KG, j % p.KG);
         __syncwarp();
     }
     // B image: entry (step s, chunk c, row n = blk * COUTP + o) holds the 8
@@ -1011,9 +1015,9 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         if (lane == 0) {
             const uint64_t vol_base = smem_addr(sVol) >> 4;
             const uint64_t b_base = smem_addr(sB) >> 4;
-            for (int it = 0; it < n_iter; ++it) {
-                const int vb = it % NV;
-                if (!wait_or_fail(smem_addr(&vol_full[vb]), (it / NV) & 1, p.err, 2)) break;
+            int vb = 0, vph = 0;  // buffer it % NV and its phase (it / NV) & 1, kept running
+            for (int it = 0; it < n_iter; ++it, (++vb == NV ? (vb = 0, vph ^= 1) : 0)) {
+                if (!wait_or_fail(smem_addr(&vol_full[vb]), vph, p.err, 2)) break;
                 const int u = u_first + it;
                 bool row_ok = true;
                 for (int grp = 0; grp < p.n_grp; ++grp) {
@@ -1057,19 +1061,25 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
             const int rbase = w0 - 8 * n_runs - p.d_off;
             const int nvr = p.rstage_w / 8;
             int issued = n_pre;  // jobs [0, n_pre) were issued during set-up
-            for (int j = n_pre; j < total_jobs; ++j) {
-                const int slot = j % NS;
-                if (j >= NS && !warp_wait(smem_addr(&stage_empty[slot]), ((j / NS) - 1) & 1, p.err, 6)) break;
+            // Running ring position of job j: slot j % NS, round j / NS, row
+            // offset j / KG, octet j % KG (no division per job).
+            int slot = n_pre == NS ? 0 : n_pre, rnd = n_pre == NS ? 1 : 0;
+            int jr = n_pre / p.KG, kg = n_pre - jr * p.KG;
+            auto advance = [&] {
+                if (++slot == NS) { slot = 0; ++rnd; }
+                if (++kg == p.KG) { kg = 0; ++jr; }
+            };
+            for (int j = n_pre; j < total_jobs; ++j, advance()) {
+                if (rnd > 0 && !warp_wait(smem_addr(&stage_empty[slot]), (rnd - 1) & 1, p.err, 6)) break;
                 issued = j + 1;
                 if (p.use_tma) {
-                    if (elect_one()) tma_job(j);
+                    if (elect_one()) tma_job(slot, jr, kg);
                     __syncwarp();
                     continue;
                 }
                 if constexpr (!FUSED) continue;  // (volume mode stages only by TMA)
                 const uint32_t sbase = smem_addr(smem + p.off_stage + slot * p.stage_slot_bytes);
-                const int urow = uv0 + j / p.KG - p.in_row0;
-                const int kg = j % p.KG;
+                const int urow = uv0 + jr - p.in_row0;
                 const uint32_t full = smem_addr(&stage_full[slot]);
                 for (int lc = lane; lc < 8 * Cg; lc += 32) {  // lc = row of the job (e * Cg + c)
                     const int ge = lc / Cg, cc = lc - ge * Cg;
@@ -1128,10 +1138,14 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
         const int pw = warp - kProdWarp0;
         const uint32_t zero_row = smem_addr(smem + p.off_zero);
         bool ok = true;
-        for (int it = 0; it < n_iter && ok; ++it) {
+        int vb = 0, vrnd = 0;  // buffer it % NV and round it / NV, kept running
+        int js = 0, jph = 0;   // slot and phase of the next staging job (jobs in order)
+        auto next_job = [&] {
+            if (++js == p.n_slots) { js = 0; jph ^= 1; }
+        };
+        for (int it = 0; it < n_iter && ok; ++it, (++vb == NV ? (vb = 0, ++vrnd) : 0)) {
             const int u = u_first + it;
-            const int vb = it % NV;
-            if (it >= NV && !warp_wait(smem_addr(&vol_empty[vb]), ((it / NV) - 1) & 1, p.err, 4)) break;
+            if (vrnd > 0 && !warp_wait(smem_addr(&vol_empty[vb]), (vrnd - 1) & 1, p.err, 4)) break;
             if (u >= 0 && u < p.H) {
                 uint8_t* vbuf = sVol + vb * p.vol_buf_bytes;
                 if (FUSED && CORR >= 6) {
@@ -1181,10 +1195,10 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     }
                 } else if (FUSED) {
                     const int job0 = (u - uv0) * p.KG;  // job of (u, octet 0)
-                    for (int kg = 0; kg < p.KG && ok; ++kg) {
+                    for (int kg = 0; kg < p.KG && ok; ++kg, next_job()) {
                         const int job = job0 + kg;
-                        const int slot = job % p.n_slots;
-                        if (!warp_wait(smem_addr(&stage_full[slot]), (job / p.n_slots) & 1, p.err, 7)) {
+                        const int slot = js;
+                        if (!warp_wait(smem_addr(&stage_full[slot]), jph, p.err, 7)) {
                             ok = false;
                             break;
                         }
@@ -1194,9 +1208,10 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                         // T = tpj * ntile tasks per job, tau % kProdWarps == pw;
                         // task h is range h % tpj of tile h / tpj.
                         const int T = p.tpj * NT;
-                        for (int h = ((pw - job * T) % kProdWarps + kProdWarps) % kProdWarps; h < T; h += kProdWarps) {
-                            const int tl = NT == 2 ? h / p.tpj : 0, hh = h - tl * p.tpj;
-                            const int jt0 = (hh * p.n_tiles) / p.tpj, jt1 = ((hh + 1) * p.n_tiles) / p.tpj;
+                        static_assert((kProdWarps & (kProdWarps - 1)) == 0, "warp rotation by mask");
+                        for (int h = (pw - job * T) & (kProdWarps - 1); h < T; h += kProdWarps) {
+                            const int tl = (NT == 2 && h >= p.tpj) ? 1 : 0, hh = h - tl * p.tpj;
+                            const int jt0 = p.task_jt[hh], jt1 = p.task_jt[hh + 1];
                             corr_task<CORR, NT>(p, sbase, zero_row, vsa + static_cast<uint32_t>(tl) * p.tile_vol_bytes,
                                                 jt0, jt1, lane, tl);
                         }
@@ -1214,10 +1229,10 @@ __global__ void __launch_bounds__(kThreads, 1) stem_tc_kernel(const __grid_const
                     const int np = p.d_hi - p.d_lo;
                     const uint32_t gbytes = static_cast<uint32_t>(np) * 48u;
                     const int job0 = (u - uv0) * p.KG;
-                    for (int kg = 0; kg < p.KG && ok; ++kg) {
+                    for (int kg = 0; kg < p.KG && ok; ++kg, next_job()) {
                         const int job = job0 + kg;
-                        const int slot = job % p.n_slots;
-                        if (!warp_wait(smem_addr(&stage_full[slot]), (job / p.n_slots) & 1, p.err, 7)) {
+                        const int slot = js;
+                        if (!warp_wait(smem_addr(&stage_full[slot]), jph, p.err, 7)) {
                             ok = false;
                             break;
                         }
@@ -1607,6 +1622,8 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
     // (and so the staging ring's turnover) short (measured: 7 % faster than
     // one tile per task on config 2, and faster on every config).
     p.tpj = (p.n_tiles + 1) / 2;
+    if (p.tpj > kMaxTasks) return WW_ERR_UNSUPPORTED;
+    for (int hh = 0; hh <= p.tpj; ++hh) p.task_jt[hh] = static_cast<uint8_t>((hh * p.n_tiles) / p.tpj);
     // CUDA-core correlation items: (right tile, volume column) pairs with
     // any disparity in [0, D), and the most jobs a task of 32 items touches.
     p.n_fitems = 0;

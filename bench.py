@@ -73,7 +73,7 @@ CORR_VOLUME_CONFIG = 2
 NCU_TRAFFIC_BYTES = {
     "c2_gwc40_stem32": 24.84e6 + 7.11e6,
     "c3_hd_gwc8_stem16": 126.54e6 + 449.70e6,
-    "c4_batched_gwc32_stem32": (274.21e6 + 687.38e6) * 8,
+    "c4_batched_gwc32_stem32": (265.48e6 + 680.47e6) * 8,
     "c5_edge_gwc16_stem16": 6.56e6 + 0.17e6,
 }
 

@@ -1616,12 +1616,16 @@ int stem_tc_launch_band(const void* vol, const void* left, const void* right, co
     // interleaved, so its MMAs stay independent).
     p.n_grp = p.ntile == 2 ? 2 : (n_mb >= kGroupMinMB ? 2 : 1);
     p.grp_size = p.ntile == 2 ? n_mb : (n_mb + p.n_grp - 1) / p.n_grp;
-    // Tasks per job: two right tiles per task.  A task loads its octet's left
-    // (A) fragments once for all its tiles, so two tiles per task halve those
-    // loads, while half the producer warps per job still keep a job's latency
-    // (and so the staging ring's turnover) short (measured: 7 % faster than
-    // one tile per task on config 2, and faster on every config).
-    p.tpj = (p.n_tiles + 1) / 2;
+    // Tasks per job: two right tiles per task with one column tile per CTA,
+    // four with two.  A task loads its octet's left (A) fragments once for all
+    // its tiles, so more tiles per task mean fewer of those loads, while
+    // enough producer warps per job keep a job's latency (and so the staging
+    // ring's turnover) short.  Measured: two tiles 7 % faster than one on
+    // config 2, three and four tiles slower on configs 2 and 4 (3 % and 5 %
+    // with four); with two column tiles (twice the tasks per job) four tiles
+    // per task are 2.5 % faster on config 3 and equal on config 5.
+    const int tiles_per_task = p.ntile == 2 ? 4 : 2;
+    p.tpj = (p.n_tiles + tiles_per_task - 1) / tiles_per_task;
     if (p.tpj > kMaxTasks) return WW_ERR_UNSUPPORTED;
     for (int hh = 0; hh <= p.tpj; ++hh) p.task_jt[hh] = static_cast<uint8_t>((hh * p.n_tiles) / p.tpj);
     // CUDA-core correlation items: (right tile, volume column) pairs with

@@ -71,10 +71,10 @@ CORR_VOLUME_CONFIG = 2
 # and 5 leave most or all of their output in L2 when the launch ends; config 4
 # is captured at B = 8 and scaled by 64 / 8 (traffic is per pair).
 NCU_TRAFFIC_BYTES = {
-    "c2_gwc40_stem32": 24.84e6 + 7.11e6,
-    "c3_hd_gwc8_stem16": 126.54e6 + 449.70e6,
+    "c2_gwc40_stem32": 24.87e6 + 7.26e6,
+    "c3_hd_gwc8_stem16": 125.60e6 + 448.59e6,
     "c4_batched_gwc32_stem32": (265.48e6 + 680.47e6) * 8,
-    "c5_edge_gwc16_stem16": 6.56e6 + 0.17e6,
+    "c5_edge_gwc16_stem16": 6.57e6 + 0.18e6,
 }
 
 # Streams the end-to-end loop rotates over (copy in, op, copy out per chunk).

@@ -107,6 +107,8 @@ int ww_cost_stem3d_ref3(const void* in, void* out,
  * tensor cores.
  * vol [B, Cin, D, H, W], w [Cout, Cin, 3, 3, 3] (BN already folded, see
  * ww_fold_bn_f16), b [Cout], out [B, Cout, D, H, W].
+ * Fastest with W % 8 == 0 and a 16-byte aligned vol (staged by TMA); any
+ * other volume is gathered element by element, with the same output.
  * ------------------------------------------------------------------------- */
 int ww_cost_stem3d(const void* vol, const void* w, const void* b, void* out,
                    int B, int Cin, int Cout, int D, int H, int W, int act, void* stream);
